@@ -1,0 +1,106 @@
+"""ctypes binding of libg4attn.so (the C ABI declared in include/g4attn.h).
+
+The library is loaded from this package directory.  There is no fallback: if the shared
+library is missing or fails to load, importing the binding raises, so a GPU run can never
+silently compute on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_size_t, c_uint32, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libg4attn.so"
+
+G4A_OK = 0
+STATUS_NAMES = {
+    0: "G4A_OK",
+    1: "G4A_EINVAL",
+    2: "G4A_ECUDA",
+    3: "G4A_ENOMEM",
+    4: "G4A_ETIMEOUT",
+    5: "G4A_ENCCL",
+    6: "G4A_EUNSUPPORTED",
+}
+
+
+class G4AError(RuntimeError):
+    """A libg4attn call returned a non-OK status."""
+
+    def __init__(self, status: int, func: str, message: str):
+        self.status = status
+        self.status_name = STATUS_NAMES.get(status, str(status))
+        self.func = func
+        super().__init__(f"{func}: {self.status_name}: {message}")
+
+
+# (name, argtypes) for every g4a_status entry point.
+_u32 = c_uint32
+_f = c_float
+_p = c_void_p
+SIGNATURES: dict[str, list] = {
+    "g4a_create": [c_int, POINTER(c_void_p)],
+    "g4a_destroy": [_p],
+    "g4a_set_stream": [_p, _p],
+    "g4a_sync": [_p, _u32],
+    "g4a_alloc": [_p, c_size_t, POINTER(c_void_p)],
+    "g4a_free": [_p, _p],
+    "g4a_memcpy_h2d": [_p, _p, _p, c_size_t],
+    "g4a_memcpy_d2h": [_p, _p, _p, c_size_t],
+    "g4a_memset": [_p, _p, c_int, c_size_t],
+    "g4a_reserve_workspace": [_p, _u32, _u32, _u32],
+    "g4a_norm_rope": [_p, _p, _p, _p, _u32, _u32, _f, _u32, _f, _u32],
+    "g4a_rms_norm_no_weight": [_p, _p, _u32, _u32, _f],
+    "g4a_kv_store": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],
+    "g4a_decode_attn": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],
+    "g4a_decode_attn_paged": [_p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _f, _u32, _p],
+    "g4a_decode_attn_partial": [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _u32, _p],
+    "g4a_lse_merge": [_p, _p, _u32, _u32, _u32, _p],
+    "g4a_attn_decode_layer": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _f, _u32, _u32, _u32,
+                              _u32, _f, _u32, _f, _u32, _u32],
+    "g4a_prefill_qkv_prep": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f,
+                             _u32],
+    "g4a_prefill_attn": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _f, _u32],
+}
+EXTRA_SYMBOLS = {"g4a_last_error": ([], c_char_p), "g4a_version": ([], c_char_p),
+                 "g4a_get_stream": ([c_void_p], c_void_p)}
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the shared library with argtypes set."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(
+            f"libg4attn.so not found at {p}; build it with `python gemma4-webgpu_b200/build.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(p))
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = c_int
+    for name, (argtypes, restype) in EXTRA_SYMBOLS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point and raise G4AError on a non-OK status."""
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != G4A_OK:
+        msg = lib.g4a_last_error()
+        raise G4AError(st, name, msg.decode() if msg else "")
+
+
+def exported_symbols() -> list[str]:
+    return sorted(list(SIGNATURES) + list(EXTRA_SYMBOLS))
