@@ -5,6 +5,7 @@
 // `deviceLost` flag checked by every public entry point (:432-435, :2214, :2509).
 #include <stdarg.h>
 #include <stdio.h>
+#include <string.h>
 
 #include <chrono>
 #include <thread>
@@ -61,7 +62,85 @@ g4a_status g4a_ensure_workspace(g4a_ctx* ctx, size_t bytes) {
   return G4A_OK;
 }
 
+const char* const g4a_prof_names[G4A_PROF_NUM_LABELS] = {
+    "norm_rope", "rms_norm_no_weight", "kv_store", "decode_prep", "decode_splitkv",
+    "decode_merge", "decode_generic", "lse_merge", "prefill_prep", "prefill_attn"};
+
+static cudaEvent_t prof_event(g4a_ctx* ctx) {
+  if (!ctx->prof_free.empty()) {
+    cudaEvent_t e = ctx->prof_free.back();
+    ctx->prof_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+g4a_prof_scope::g4a_prof_scope(g4a_ctx* c, int l) : ctx(c), label(l) {
+  if (!ctx || !ctx->prof_enabled) return;
+  cudaEvent_t b = prof_event(ctx);
+  end = prof_event(ctx);
+  if (!b || !end) {
+    end = nullptr;
+    return;
+  }
+  cudaEventRecord(b, ctx->stream);
+  ctx->prof_pending.push_back({label, b, end});
+}
+
+g4a_prof_scope::~g4a_prof_scope() {
+  if (end) cudaEventRecord(end, ctx->stream);
+}
+
+// Fold completed event pairs into the per-label totals (waits for the stream).
+static g4a_status prof_collect(g4a_ctx* ctx) {
+  if (ctx->prof_pending.empty()) return G4A_OK;
+  G4A_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  for (auto& r : ctx->prof_pending) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, r.begin, r.end) == cudaSuccess) {
+      ctx->prof_ms[r.label] += ms;
+      ctx->prof_count[r.label] += 1;
+    }
+    ctx->prof_free.push_back(r.begin);
+    ctx->prof_free.push_back(r.end);
+  }
+  ctx->prof_pending.clear();
+  return G4A_OK;
+}
+
 extern "C" {
+
+g4a_status g4a_profile_enable(g4a_ctx* ctx, int enable) {
+  G4A_CHECK_CTX(ctx);
+  ctx->prof_enabled = enable != 0;
+  return G4A_OK;
+}
+
+g4a_status g4a_profile_reset(g4a_ctx* ctx) {
+  G4A_CHECK_CTX(ctx);
+  if (g4a_status s = prof_collect(ctx)) return s;
+  for (int i = 0; i < G4A_PROF_NUM_LABELS; i++) {
+    ctx->prof_ms[i] = 0.0;
+    ctx->prof_count[i] = 0;
+  }
+  return G4A_OK;
+}
+
+g4a_status g4a_profile_read(g4a_ctx* ctx, const char* label, double* total_ms, uint64_t* count) {
+  G4A_CHECK_CTX(ctx);
+  if (!label || !total_ms || !count) return g4a_fail(G4A_EINVAL, "g4a_profile_read: null argument");
+  if (g4a_status s = prof_collect(ctx)) return s;
+  for (int i = 0; i < G4A_PROF_NUM_LABELS; i++) {
+    if (strcmp(label, g4a_prof_names[i]) == 0) {
+      *total_ms = ctx->prof_ms[i];
+      *count = ctx->prof_count[i];
+      return G4A_OK;
+    }
+  }
+  return g4a_fail(G4A_EINVAL, "g4a_profile_read: unknown label '%s'", label);
+}
 
 const char* g4a_last_error(void) { return t_last_error.c_str(); }
 
@@ -116,6 +195,11 @@ g4a_status g4a_destroy(g4a_ctx* ctx) {
   if (ctx == nullptr) return G4A_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (auto& r : ctx->prof_pending) {
+    cudaEventDestroy(r.begin);
+    cudaEventDestroy(r.end);
+  }
+  for (auto e : ctx->prof_free) cudaEventDestroy(e);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->sync_event) cudaEventDestroy(ctx->sync_event);
   if (ctx->dev_err_host) cudaFreeHost((void*)ctx->dev_err_host);

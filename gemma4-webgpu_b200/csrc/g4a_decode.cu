@@ -722,6 +722,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   p.seg_range = reinterpret_cast<int2*>(reinterpret_cast<char*>(ctx->workspace) + part_bytes);
   p.err = ctx->dev_err_dev;
   if (stages_upper > 0) {
+    g4a_prof_scope ps(ctx, G4A_PROF_DECODE_SPLITKV);
     cudaError_t e = g4a_launch(decode_splitkv_kernel<HD>, dim3(grid), dim3(kThreads), C::SMEM, ctx->stream, pdl, p);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch decode_splitkv_kernel");
   }
@@ -729,6 +730,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   // and always in partial mode.
   const bool need_merge = (mode == 1) || grid > 1 || stages_upper == 0 || P > 1;
   if (need_merge) {
+    g4a_prof_scope ps(ctx, G4A_PROF_DECODE_MERGE);
     cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 64), dim3(256), 0, ctx->stream,
                                stages_upper > 0, p, mode, part_out);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch merge_segments_kernel");
@@ -790,6 +792,7 @@ g4a_status decode_contiguous(g4a_ctx* ctx, const float* q, const uint16_t* k, co
   const uint32_t ws = (window != 0u && kv_len > window) ? kv_len - window : 0u;
   const long long keys = (long long)(kv_len - ws);
   if (fast_path_ok(nqh, nkh, hd)) return dispatch_fast(ctx, p, keys * nkh + (long long)(nkh - 1) * kps_of(hd), 0, nullptr, pdl);
+  g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<nqh, 256, 0, ctx->stream>>>(p, 0, nullptr);
   return g4a_check_launch("decode_generic_kernel");
 }
@@ -849,6 +852,7 @@ g4a_status g4a_decode_attn_paged(g4a_ctx* ctx, const float* q, const uint16_t* k
     keys = keys * num_kv_heads + (long long)batch * num_kv_heads * kps_of(head_dim);
     return dispatch_fast(ctx, p, keys, 0, nullptr, false);
   }
+  g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<batch * num_q_heads, 256, 0, ctx->stream>>>(p, 0, nullptr);
   return g4a_check_launch("decode_generic_kernel");
 }
@@ -872,6 +876,7 @@ g4a_status g4a_decode_attn_partial(g4a_ctx* ctx, const float* q, const uint16_t*
   const long long keys = hi > lo ? (long long)(hi - lo) : 0;
   if (num_kv_heads == 1 && fast_path_ok(num_q_heads, num_kv_heads, head_dim))
     return dispatch_fast(ctx, p, keys, 1, part, false);
+  g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<num_q_heads, 256, 0, ctx->stream>>>(p, 1, part);
   return g4a_check_launch("decode_generic_kernel(partial)");
 }
@@ -882,6 +887,7 @@ g4a_status g4a_lse_merge(g4a_ctx* ctx, const float* parts, uint32_t n_parts, uin
   if (!parts || !out) return g4a_fail(G4A_EINVAL, "g4a_lse_merge: null pointer");
   if (n_parts == 0 || num_q_heads == 0 || head_dim == 0)
     return g4a_fail(G4A_EINVAL, "g4a_lse_merge: n_parts, num_q_heads and head_dim must be > 0");
+  g4a_prof_scope ps(ctx, G4A_PROF_LSE_MERGE);
   lse_merge_kernel<<<num_q_heads, 256, 0, ctx->stream>>>(parts, (int)n_parts, (int)num_q_heads, (int)head_dim, out);
   return g4a_check_launch("lse_merge_kernel");
 }

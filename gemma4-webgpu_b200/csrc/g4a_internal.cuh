@@ -6,8 +6,32 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "g4attn.h"
+
+// Kernel labels of the per-kernel profiler (CUDA events around each launch, aggregated per
+// label), the counterpart of the reference's per-pass timestamp queries
+// (src/engine.ts:3208-3285).
+enum g4a_prof_label : int {
+  G4A_PROF_NORM_ROPE = 0,
+  G4A_PROF_RMS_NORM,
+  G4A_PROF_KV_STORE,
+  G4A_PROF_DECODE_PREP,
+  G4A_PROF_DECODE_SPLITKV,
+  G4A_PROF_DECODE_MERGE,
+  G4A_PROF_DECODE_GENERIC,
+  G4A_PROF_LSE_MERGE,
+  G4A_PROF_PREFILL_PREP,
+  G4A_PROF_PREFILL_ATTN,
+  G4A_PROF_NUM_LABELS
+};
+extern const char* const g4a_prof_names[G4A_PROF_NUM_LABELS];
+
+struct g4a_prof_rec {
+  int label;
+  cudaEvent_t begin, end;
+};
 
 // ----------------------------------------------------------------------------- host side
 
@@ -29,6 +53,21 @@ struct g4a_ctx {
   cudaEvent_t sync_event = nullptr;
   // Tensor-map encoder from the driver (for the prefill kernel), resolved on first use.
   void* encode_tiled = nullptr;
+  // Profiler state: pending event pairs, free events, per-label totals.
+  bool prof_enabled = false;
+  std::vector<g4a_prof_rec> prof_pending;
+  std::vector<cudaEvent_t> prof_free;
+  double prof_ms[G4A_PROF_NUM_LABELS] = {};
+  uint64_t prof_count[G4A_PROF_NUM_LABELS] = {};
+};
+
+// Record a begin/end event pair around a launch when profiling is on (no-op otherwise).
+struct g4a_prof_scope {
+  g4a_ctx* ctx;
+  int label;
+  cudaEvent_t end = nullptr;
+  g4a_prof_scope(g4a_ctx* c, int l);
+  ~g4a_prof_scope();
 };
 
 // Per-thread last-error message (set by every failing entry point).

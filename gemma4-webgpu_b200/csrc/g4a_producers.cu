@@ -210,6 +210,7 @@ g4a_status g4a_norm_rope(g4a_ctx* ctx, float* x, const uint16_t* weight, const u
   if (!x || !weight) return g4a_fail(G4A_EINVAL, "g4a_norm_rope: null x or weight");
   if (apply_divisor && !rope_freqs)
     return g4a_fail(G4A_EINVAL, "g4a_norm_rope: apply_divisor set but rope_freqs is null");
+  g4a_prof_scope ps(ctx, G4A_PROF_NORM_ROPE);
   norm_rope_kernel<<<num_heads, kWG, 0, ctx->stream>>>(x, (const __half*)weight, (const __half*)rope_freqs,
                                                        (int)head_dim, eps, position, theta, apply_divisor);
   return g4a_check_launch("norm_rope_kernel");
@@ -220,6 +221,7 @@ g4a_status g4a_rms_norm_no_weight(g4a_ctx* ctx, float* x, uint32_t num_heads, ui
   if (g4a_status s = check_head_dim(__func__, head_dim, false)) return s;
   if (num_heads == 0) return G4A_OK;
   if (!x) return g4a_fail(G4A_EINVAL, "g4a_rms_norm_no_weight: null x");
+  g4a_prof_scope ps(ctx, G4A_PROF_RMS_NORM);
   rms_norm_no_weight_kernel<<<num_heads, kWG, 0, ctx->stream>>>(x, (int)head_dim, eps);
   return g4a_check_launch("rms_norm_no_weight_kernel");
 }
@@ -232,6 +234,7 @@ g4a_status g4a_kv_store(g4a_ctx* ctx, const float* k, float* v, uint16_t* k_cach
   if (num_kv_heads == 0) return G4A_OK;
   if (!k || !v || !k_cache || !v_cache) return g4a_fail(G4A_EINVAL, "g4a_kv_store: null pointer");
   if (slot >= max_seq_len) return g4a_fail(G4A_EINVAL, "g4a_kv_store: slot %u >= max_seq_len %u", slot, max_seq_len);
+  g4a_prof_scope ps(ctx, G4A_PROF_KV_STORE);
   kv_store_kernel<<<num_kv_heads, kWG, 0, ctx->stream>>>(k, v, (__half*)k_cache, (__half*)v_cache, (int)num_kv_heads,
                                                          (int)head_dim, slot, eps, fuse_v_norm ? 1 : 0);
   return g4a_check_launch("kv_store_kernel");
@@ -255,6 +258,7 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
                     max_seq_len);
   if (T > 65535u) return g4a_fail(G4A_EINVAL, "g4a_prefill_qkv_prep: T %u > 65535 per call", T);
   dim3 grid(num_q_heads + num_kv_heads, T);
+  g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_PREP);
   prefill_prep_kernel<<<grid, kWG, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
                                                      (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
                                                      (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads,
@@ -273,6 +277,7 @@ g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, float* q, float* k, float* v, co
   if (g4a_status s = check_head_dim("g4a_attn_decode_layer", hd, true)) return s;
   uint32_t blocks = nqh + (is_producer ? nkh : 0u);
   if (blocks == 0) return G4A_OK;
+  g4a_prof_scope ps(ctx, G4A_PROF_DECODE_PREP);
   decode_prep_kernel<<<blocks, kWG, 0, ctx->stream>>>(q, k, v, (const __half*)qw, (const __half*)kw,
                                                       (const __half*)rope_freqs, (__half*)k_cache,
                                                       (__half*)v_cache, (int)nqh, (int)nkh, (int)hd, eps, position,

@@ -101,6 +101,20 @@ class Context:
     def reserve_workspace(self, max_batch: int, head_dim: int, num_q_heads: int) -> None:
         call("g4a_reserve_workspace", self._h, max_batch, head_dim, num_q_heads)
 
+    # ---------------------------------------------------------------- profiler
+    def profile_enable(self, on: bool = True) -> None:
+        call("g4a_profile_enable", self._h, 1 if on else 0)
+
+    def profile_reset(self) -> None:
+        call("g4a_profile_reset", self._h)
+
+    def profile_read(self, label: str) -> tuple[float, int]:
+        """(total device ms, launches) of one kernel label since the last reset."""
+        ms = ctypes.c_double()
+        n = ctypes.c_uint64()
+        call("g4a_profile_read", self._h, label.encode(), ctypes.byref(ms), ctypes.byref(n))
+        return ms.value, n.value
+
     # ---------------------------------------------------------------- producers
     def norm_rope(self, x, weight, rope_freqs=None, *, num_heads, head_dim, eps, position, theta,
                   apply_divisor=0) -> None:

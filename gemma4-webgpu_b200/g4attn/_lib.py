@@ -50,6 +50,9 @@ SIGNATURES: dict[str, list] = {
     "g4a_memcpy_d2h": [_p, _p, _p, c_size_t],
     "g4a_memset": [_p, _p, c_int, c_size_t],
     "g4a_reserve_workspace": [_p, _u32, _u32, _u32],
+    "g4a_profile_enable": [_p, c_int],
+    "g4a_profile_reset": [_p],
+    "g4a_profile_read": [_p, c_char_p, POINTER(ctypes.c_double), POINTER(ctypes.c_uint64)],
     "g4a_norm_rope": [_p, _p, _p, _p, _u32, _u32, _f, _u32, _f, _u32],
     "g4a_rms_norm_no_weight": [_p, _p, _u32, _u32, _f],
     "g4a_kv_store": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],

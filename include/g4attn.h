@@ -92,6 +92,16 @@ g4a_status g4a_memset(g4a_ctx* ctx, void* dst_device, int value, size_t bytes);
 g4a_status g4a_reserve_workspace(g4a_ctx* ctx, uint32_t max_batch, uint32_t head_dim,
                                  uint32_t num_q_heads);
 
+/* Per-kernel profiler: when enabled, every kernel launch is bracketed by CUDA events and its
+ * device time is summed per label ("norm_rope", "rms_norm_no_weight", "kv_store",
+ * "decode_prep", "decode_splitkv", "decode_merge", "decode_generic", "lse_merge",
+ * "prefill_prep", "prefill_attn").  Counterpart of the reference's per-pass timestamp
+ * queries (src/engine.ts:3208-3285, src/diagnostics/profile.ts:48-132).  Reading waits for
+ * the context's stream.  Leave it off for timing whole steps: the events serialise launches. */
+g4a_status g4a_profile_enable(g4a_ctx* ctx, int enable);
+g4a_status g4a_profile_reset(g4a_ctx* ctx);
+g4a_status g4a_profile_read(g4a_ctx* ctx, const char* label, double* total_ms, uint64_t* count);
+
 /* ------------------------------------------------------------------ producers */
 
 /* Per-head RMSNorm with an f16 weight, then NeoX half-split RoPE, in place on x
