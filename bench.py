@@ -1,0 +1,493 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention hot path: decode-attention KV GB/s and µs/layer.
+
+Workload (the metric's configuration): single-sequence decode attention on a
+global Gemma layer -- 8 q heads, 1 KV head, head_dim 256, f16 KV cache of L = 32768 tokens,
+theta 1e6, scale 1.0, f32 output.  The caches are built on the GPU by the library's own producer
+kernels (norm+RoPE for K, weightless v_norm for V) from seeded N(0,1) raw rows.
+
+A step is one decode token through R = 16 such layers, each with its own cache (16 x 33.6 MB =
+537 MB, more than the 126 MB L2, so every layer-call reads its KV from HBM).  The timed region
+replays a CUDA graph of one step K times; value = algorithmic KV bytes / device time, summed
+over ranks (each rank runs its own independent sequences: weak scaling, no collective).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Besides `value` the line carries: `roofline` (the split-KV kernel's achieved GB/s from live
+CUDA events vs the measured HBM copy peak, DRAM traffic from the committed ncu summary),
+`e2e` (same metric through the C ABI with pinned host buffers copied in and out every layer
+call), `cpu_baseline` (the CPU restatement of the reference chain on the host cores), `clocks`
+(nvidia-smi samples during the timed region) and `sweep` (4k / 128k contexts, N=1).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import ctypes
+import datetime
+import io
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "gemma4-webgpu_b200"), str(ROOT)]
+
+METRIC = "decode-attn KV GB/s (% of HBM peak) and µs/layer at 1/2/4/8 B200"
+NQH, NKH, HD = 8, 1, 256
+EPS = 1e-6
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--kv-len", type=int, default=32768)
+    ap.add_argument("--layers", type=int, default=16, help="distinct layer caches per step")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def kv_bytes(L: int, window: int = 0) -> int:
+    vis = min(L, window) if window else L
+    return 2 * vis * NKH * HD * 2 + 2 * NQH * HD * 4
+
+
+def ncu_traffic(kernel_file: str):
+    """DRAM bytes per launch recorded in the committed ncu summary, or None."""
+    f = ROOT / "profiles" / kernel_file
+    if not f.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch\s*[=:]\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu=timestamp,{self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def mark_begin(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for r in csv.reader(io.StringIO(out)):
+            if len(r) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                continue
+            rows.append((ts, [x.strip() for x in r[1:]]))
+        inside = [x for t, x in rows if self.t0 and self.t1 and self.t0 <= t <= self.t1]
+        window = "timed"
+        if not inside:  # timed region shorter than the sampling period: nearest samples
+            window = "nearest"
+            inside = [x for _, x in rows[-3:]]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [num(x[1]) for x in inside if num(x[1]) is not None]
+        mx = [num(x[2]) for x in inside if num(x[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for x in inside for i in range(4) if x[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(inside), "window": window,
+                "power_w_max": max((num(x[3]) or 0.0) for x in inside)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ----------------------------------------------------------------------------- setup
+def build_layers(ctx, torch, L: int, R: int, seed: int):
+    """R layer caches [L, 1, 256] f16 built by the producer kernels, and R roped queries."""
+    import numpy as np
+
+    from g4attn import synth
+
+    dev = torch.device("cuda", ctx.device)
+    kcs, vcs, qs = [], [], []
+    dummy = torch.zeros(16, device=dev)
+    dummy16 = torch.zeros(16, dtype=torch.float16, device=dev)
+    for r in range(R):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed * 1000 + r)
+        rng = np.random.default_rng(seed * 1000 + r)
+        qw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).to(dev).view(torch.float16)
+        kw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).to(dev).view(torch.float16)
+        kc = torch.empty((L, NKH, HD), dtype=torch.float16, device=dev)
+        vc = torch.empty_like(kc)
+        for c0 in range(0, L, 32768):
+            T = min(32768, L - c0)
+            k = torch.randn((T, NKH, HD), generator=g, device=dev)
+            v = torch.randn((T, NKH, HD), generator=g, device=dev)
+            ctx.prefill_qkv_prep(dummy, k, v, kw, kw, None, dummy16, kc, vc, T=T, start_pos=c0, max_seq_len=L,
+                                 num_q_heads=0, num_kv_heads=NKH, head_dim=HD, eps=EPS, theta=1e6)
+        q = torch.randn((NQH, HD), generator=g, device=dev)
+        ctx.norm_rope(q, qw, None, num_heads=NQH, head_dim=HD, eps=EPS, position=L - 1, theta=1e6)
+        kcs.append(kc)
+        vcs.append(vc)
+        qs.append(q)
+    ctx.sync()
+    return kcs, vcs, qs
+
+
+def layers_for(L: int, cap: int = 64) -> int:
+    per = kv_bytes(L)
+    return max(2, min(cap, math.ceil(4 * L2_BYTES / per)))
+
+
+def time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, steps, warmup):
+    """Capture one step (one call per layer cache) in a CUDA graph; replay warmup + steps times.
+    Returns device ms for the timed steps."""
+    R = len(kcs)
+
+    def one_step():
+        for r in range(R):
+            ctx.decode_attn(qs[r], kcs[r], vcs[r], outs[r], num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                            seq_len=L, scale=1.0, sliding_window=0)
+
+    one_step()  # configures kernels, sizes the workspace outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ctx.set_stream(s.cuda_stream)
+        with torch.cuda.graph(g, stream=s):
+            one_step()
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    return g
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    orc.lib()
+    nthreads = os.cpu_count() or 1
+    orc.set_num_threads(nthreads)
+    L = args.kv_len
+    rng = np.random.default_rng(1)
+    q = rng.standard_normal((NQH, HD)).astype(np.float32)
+    q /= np.sqrt((q * q).mean(-1, keepdims=True))
+    k = orc.f16_to_f32(orc.f32_to_f16(rng.standard_normal((L, NKH, HD)).astype(np.float32)))
+    v = orc.f16_to_f32(orc.f32_to_f16(rng.standard_normal((L, NKH, HD)).astype(np.float32)))
+
+    def call(n):
+        return orc.decode_chain_f32(q, k[:n], v[:n], num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=n)
+
+    t = time.perf_counter()
+    call(L)
+    t_full = time.perf_counter() - t
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    n = L if t_full <= budget else max(256, int(L * budget / t_full))
+    for _ in range(args.warmup):
+        call(n)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        call(n)
+    dt = time.perf_counter() - t
+    gbs = kv_bytes(n) * args.steps / dt / 1e9
+    line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"config[1] global decode, 8q/1kv heads, head_dim 256, kv_len {L}",
+                       "kv_len_per_step": n},
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": nthreads, "kind": "port",
+                             "sample": f"reference chain attn_score->softmax->attn_output (WGSL order, f32 caches) "
+                                       f"over {n} of {L} keys per step, OpenMP {nthreads} threads"},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline(L: int, seconds: float):
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    orc.lib()
+    nthreads = os.cpu_count() or 1
+    orc.set_num_threads(nthreads)
+    rng = np.random.default_rng(1)
+    q = rng.standard_normal((NQH, HD)).astype(np.float32)
+    q /= np.sqrt((q * q).mean(-1, keepdims=True))
+    k = orc.f16_to_f32(orc.f32_to_f16(rng.standard_normal((L, NKH, HD)).astype(np.float32)))
+    v = orc.f16_to_f32(orc.f32_to_f16(rng.standard_normal((L, NKH, HD)).astype(np.float32)))
+    orc.decode_chain_f32(q, k, v, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        t = time.perf_counter()
+        orc.decode_chain_f32(q, k, v, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+        times.append(time.perf_counter() - t)
+    med = statistics.median(times)
+    return {"value": kv_bytes(L) / med / 1e9, "unit": "GB/s", "cores": nthreads, "kind": "port",
+            "sample": f"{len(times)} layer-calls at kv_len {L}: reference chain attn_score->softmax->attn_output "
+                      f"restated in C (WGSL order, f32 caches), OpenMP, median",
+            "us_per_layer": med * 1e6}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    import g4attn
+
+    ctx = g4attn.Context(local)
+    L, R = args.kv_len, args.layers
+    per_layer = kv_bytes(L)
+    if per_layer * R < 2 * L2_BYTES:
+        R = layers_for(L)
+    kcs, vcs, qs = build_layers(ctx, torch, L, R, seed=1 + rank)
+    outs = [torch.zeros((NQH, HD), device="cuda") for _ in range(R)]
+    ctx.reserve_workspace(1, HD, NQH)
+    graph = time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, args.steps, args.warmup)
+
+    clock = ClockSampler(physical_gpu_index(local))
+    clock.start()
+    time.sleep(0.3)
+    # ---- timed region: K steps of R layer-calls
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clock.mark_begin()
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    clock.mark_end()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    clocks = clock.stop()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    total_bytes = per_layer * R * args.steps * world
+    value = total_bytes / (ms / 1e3) / 1e9
+    us_per_layer = ms_per_step * 1e3 / R
+    hbm, _, peak_kind = peaks()
+
+    # ---- kernel-level roofline: same steps with the per-kernel profiler (events per launch)
+    ctx.profile_reset()
+    ctx.profile_enable(True)
+    n_prof = max(1, min(args.steps, 64))
+    for _ in range(n_prof):
+        for r in range(R):
+            ctx.decode_attn(qs[r], kcs[r], vcs[r], outs[r], num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                            seq_len=L)
+    ctx.sync()
+    k_ms, k_n = ctx.profile_read("decode_splitkv")
+    m_ms, m_n = ctx.profile_read("decode_merge")
+    ctx.profile_enable(False)
+    k_avg_us = k_ms / max(k_n, 1) * 1e3
+    achieved = per_layer / (k_avg_us * 1e-6) / 1e9
+    launches_per_layer = (1 if k_n else 0) + (1 if m_n else 0)
+
+    # ---- end to end through the C ABI with pinned host buffers
+    e2e = run_e2e(ctx, torch, kcs, vcs, L, R, min(args.steps * R, 4000), rank)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "us_per_layer": us_per_layer,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config[1] global decode: 8 q heads / 1 kv head, head_dim 256, f16 KV cache, "
+                               f"kv_len {L}, theta 1e6, scale 1.0, f32 out",
+                   "kv_len": L, "layers_per_step": R, "kv_dtype": "f16",
+                   "l2": f"inputs larger than L2: {R} distinct layer caches ({R * per_layer / 2**20:.0f} MiB) "
+                         f"rotated every step",
+                   "global_batch": world, "seq_len": L,
+                   "parallelism": f"replicas{world}: independent sequences per GPU, no collective",
+                   "timing": "CUDA graph of one step replayed K times, CUDA events, max over ranks"},
+        "hbm_frac_of_measured": value / world / hbm,
+        "hbm_frac_of_nominal_8tbs": value / world / 8000.0,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": peak_kind, "kernel": "decode_splitkv_kernel<256>",
+                     "kernel_us": k_avg_us, "merge_us": m_ms / max(m_n, 1) * 1e3,
+                     "algorithmic_bytes_per_launch": per_layer,
+                     "traffic": ncu_traffic("decode_splitkv_hd256_L32768.md") if L == 32768 else None,
+                     "step_frac": value / world / hbm},
+        "gpu_launches": launches_per_layer * R * args.steps,
+        "clocks": clocks,
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_sweep:
+        line["sweep"] = run_sweep(ctx, torch, args)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(L, args.cpu_seconds)
+    del graph
+    ctx.sync()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
+def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank):
+    """The reference-facing path: pinned host q/k/v in, g4a_attn_decode_layer (producers +
+    attention), host out back, for every layer call, through the raw C ABI."""
+    import numpy as np
+
+    from g4attn import _ptr
+    from g4attn._lib import call
+
+    dev = torch.device("cuda", ctx.device)
+    rng = np.random.default_rng(100 + rank)
+    hq = torch.from_numpy(rng.standard_normal((NQH, HD)).astype(np.float32)).pin_memory()
+    hk = torch.from_numpy(rng.standard_normal((NKH, HD)).astype(np.float32)).pin_memory()
+    hv = torch.from_numpy(rng.standard_normal((NKH, HD)).astype(np.float32)).pin_memory()
+    hout = torch.zeros((NQH, HD), dtype=torch.float32).pin_memory()
+    q, k, v = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
+    out = torch.empty((NQH, HD), device=dev)
+    w = torch.ones(HD, dtype=torch.float16, device=dev)
+    h = ctx.handle
+    nb = lambda t: t.numel() * t.element_size()  # noqa: E731
+
+    def layer_call(r):
+        call("g4a_memcpy_h2d", h, _ptr(q), _ptr(hq.data_ptr()), nb(hq))
+        call("g4a_memcpy_h2d", h, _ptr(k), _ptr(hk.data_ptr()), nb(hk))
+        call("g4a_memcpy_h2d", h, _ptr(v), _ptr(hv.data_ptr()), nb(hv))
+        call("g4a_attn_decode_layer", h, _ptr(q), _ptr(k), _ptr(v), _ptr(w), _ptr(w), _ptr(None), _ptr(kcs[r]),
+             _ptr(vcs[r]), _ptr(out), NQH, NKH, HD, EPS, L - 1, L - 1, L, L, 1e6, 0, 1.0, 0, 1)
+        call("g4a_memcpy_d2h", h, _ptr(hout.data_ptr()), _ptr(out), nb(out))
+
+    for i in range(min(R, 8)):
+        layer_call(i % R)
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(calls):
+        layer_call(i % R)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert np.isfinite(hout.numpy()).all()
+    return {"value": kv_bytes(L) * calls / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "h2d_bytes_per_step": nb(hq) + nb(hk) + nb(hv), "d2h_bytes_per_step": nb(hout),
+            "us_per_layer": ms * 1e3 / calls, "layer_calls": calls,
+            "path": "g4a_memcpy_h2d x3 + g4a_attn_decode_layer (q/k norm+RoPE, v_norm, store, attention) + "
+                    "g4a_memcpy_d2h per layer call, pinned host buffers"}
+
+
+def run_sweep(ctx, torch, args):
+    out = {}
+    for L in (4096, 131072):
+        R = layers_for(L)
+        kcs, vcs, qs = build_layers(ctx, torch, L, R, seed=7)
+        outs = [torch.zeros((NQH, HD), device="cuda") for _ in range(R)]
+        g = time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, 0, 3)
+        steps = max(3, min(200, int(2e5 / R / max(L / 4096, 1))))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (steps * R)
+        hbm, _, _ = peaks()
+        gbs = kv_bytes(L) / (us * 1e-6) / 1e9
+        out[str(L)] = {"us_per_layer": us, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm, "layers": R,
+                       "steps": steps}
+        del g, kcs, vcs
+        torch.cuda.empty_cache()
+    return out
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
