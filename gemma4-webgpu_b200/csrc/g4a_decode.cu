@@ -211,11 +211,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
     for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
     S += n;
   }
-  const long long G = gridDim.x;
+  // Only the first min(grid, S) CTAs take part, so every active CTA owns at least one stage and
+  // the segment ids blockIdx.x + problem of one problem form a gap-free range.
+  const long long G = (long long)gridDim.x < S ? (long long)gridDim.x : S;
+  if ((long long)blockIdx.x >= G) return;  // uniform across the CTA
   const long long s0 = (long long)blockIdx.x * S / G;
   const long long s1 = (long long)(blockIdx.x + 1) * S / G;
   const int my_stages = (int)(s1 - s0);
-  if (my_stages <= 0) return;  // uniform across the CTA
 
   // =========================== producer role (warp 0 issues the TMA copies)
   // Stage n of this CTA goes to slot n % kStages.  Warp 0 keeps the cursor (problem, stage
@@ -551,7 +553,8 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams 
   for (int s = r.x + sg; s <= r.y; s += 16) {
     const float* row = p.part + (size_t)s * prow;
     const float ms = row[h];
-    const float sc = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+    if (ms == -INFINITY) continue;  // empty segment: contributes nothing (its o is not read)
+    const float sc = exp2f(ms - M);
     const float4 o = *reinterpret_cast<const float4*>(row + 2 * kGroup + h * hd + d);
     acc.x += sc * o.x;
     acc.y += sc * o.y;
