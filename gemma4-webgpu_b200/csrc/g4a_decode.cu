@@ -10,23 +10,25 @@
 //     (attn_score.wgsl:39); output f32 [NQH, HD] (attn_output.wgsl:22); L = 0 gives zeros.
 //
 // Fast path (NQH = 8 * NKH, HD in {128, 256, 512}): persistent CTAs, one per SM, 8 warps.
-// The flattened list of 32-key (16 for HD 512) "stages" of every (sequence, kv head) problem is
+// The flattened list of "stages" (64 keys for HD 256) of every (sequence, kv head) problem is
 // split evenly over the grid, so a CTA may cover the end of one problem and the start of the
-// next.  Warp 0 is also the producer: it TMA-bulk-copies each stage's K and V rows (one copy per
-// contiguous run of rows, no multicast) from HBM into a 4-deep shared-memory ring guarded by
-// mbarriers.  All eight warps are consumers: each owns G = 4 keys of every stage and HPW q heads
-// (8, or 4 for HD 512); a lane holds HD/32 dims of q and of the output accumulator for each of
-// its heads in registers, so one 16-byte shared load feeds HPW*HD/64 packed f32x2 FMAs.  Scores
-// are reduced across lanes with a transposing butterfly (31 shuffles per 4 keys for 8 heads),
-// then an online softmax in base 2 with lazy rescaling (the running max is only raised when a
-// score exceeds it by more than 2^8), and p*V accumulates into the registers.  At the end of
-// each segment (a problem's stages inside one CTA) the 8 warps merge through shared memory and
-// write either the final row (segment = whole problem) or an un-normalised partial (m, l, o)
-// that the merge kernel combines.  Decode is a GEMV per KV row (8 FLOP per byte of f16 KV), so
-// it stays on the CUDA cores, bound by HBM bandwidth.
+// next.  Warp 0 is also the producer: it TMA-bulk-copies every K and V row of a stage (no
+// multicast) from HBM into a 3-deep ring of padded shared-memory rows guarded by mbarriers.
+// The two contractions run on the tensor cores (mma.sync m16n8k16, f32 accumulate): q is split
+// into f16 hi + lo halves stacked as the 16 rows of the A operand, and so are the softmax
+// probabilities, which keeps ~22 significant bits through f16 operands.  Decode has only 8 query
+// rows per kv head (16 with the split), below the 64-row minimum of tcgen05.mma, and is HBM-bound;
+// on the CUDA cores the 8 FLOP per KV byte would need ~70% of the FP32 pipe at the HBM roofline
+// (measured: the CUDA-core version of this kernel reached 23% of HBM with the FMA pipe as the
+// ceiling).  Online softmax in base 2 with lazy rescaling (the running max is only raised when a
+// score exceeds it by more than 2^8).  At the end of each segment (a problem's stages inside one
+// CTA) the key groups merge through shared memory and write either the final row (segment =
+// whole problem) or an un-normalised partial (m, l, o) that the merge kernel combines.
 #include <math.h>
 
 #include <algorithm>
+
+#include <cudaTypedefs.h>
 
 #include "g4a_internal.cuh"
 
@@ -35,8 +37,6 @@ namespace {
 constexpr int kGroup = 8;  // q heads per kv head on the fast path
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;  // 2 warps per SM sub-partition: up to 255 registers each
-constexpr int kStages = 4;
-constexpr int kG = 4;                  // keys per consumer warp per stage
 constexpr float kLazyRescale = 8.0f;   // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -44,8 +44,9 @@ enum : int { F_SEG_FIRST = 1, F_SEG_LAST = 2, F_PROB_FIRST = 4, F_PROB_LAST = 8 
 
 struct StageMeta {
   int problem;
-  int key0;    // first key (position) of the stage
-  int nvalid;  // valid keys in the stage
+  int key0;    // first position of the stage (a multiple of the stage size)
+  int kfirst;  // valid rows of the stage are [kfirst, kend)
+  int kend;
   int flags;
   int seg;
 };
@@ -105,83 +106,116 @@ __device__ __forceinline__ const __half* row_ptr(const DecodeParams& p, const __
   return base + (abs_row * p.nkh + kvh) * p.hd;
 }
 
+// Tile shape of the tensor-core decode kernel for one head_dim.  The 8 warps of a CTA form NKG
+// key groups of 16 keys x NDQ slices of DPW output dims: every warp computes the scores of its
+// key group (the NDQ warps of a group compute identical scores on the tensor cores, which have
+// throughput to spare) and accumulates p*V for its DPW output dims.  A stage holds KPS keys of
+// K and of V as HD/64 column boxes of [KPS rows x 128 B] each, written by TMA with the 128-byte
+// swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7)), so ldmatrix reads of 8 rows
+// hit 8 different bank groups without padding.
 template <int HD>
 struct Cfg {
-  static constexpr int HPW = (HD <= 256) ? 8 : 4;  // q heads per consumer warp
-  static constexpr int NHW = kGroup / HPW;         // head groups
-  static constexpr int NKW = kWarps / NHW;         // key warps per head group
-  static constexpr int KPS = kG * NKW;             // keys per stage
-  static constexpr int DPL = HD / 32;              // dims per lane
-  static constexpr int NV = HPW * kG;              // score partials per lane
-  static constexpr int DUP = 32 / NV;              // lanes holding the same reduced score
-  static constexpr int ROW_BYTES = HD * 2;
-  static constexpr int STAGE_BYTES = KPS * ROW_BYTES;  // per tensor
-  static constexpr int OBUF_FLOATS = kWarps * HPW * HD;
-  static constexpr size_t SMEM = (size_t)kStages * 2 * STAGE_BYTES + OBUF_FLOATS * 4 + kWarps * HPW * 2 * 4 +
-                                 kWarps * (NV + HPW) * 4 + kStages * sizeof(StageMeta) + 2 * kStages * 8 + 64;
-  static_assert(NV == 32 || NV == 16, "reduction assumes 16 or 32 partials per lane");
+  static constexpr int NDQ = (HD == 128) ? 2 : 4;      // output-dim slices
+  static constexpr int DPW = HD / NDQ;                 // output dims per warp
+  static constexpr int NT = DPW / 8;                   // n-tiles of the p*V MMA per warp
+  static constexpr int NKG = kWarps / NDQ;             // key groups of 16 keys
+  static constexpr int KPS = 16 * NKG;                 // keys per stage
+  static constexpr int KSTEPS = HD / 16;               // k-steps of the score MMA
+  static constexpr int NCB = HD / 64;                  // 64-dim column boxes per row
+  static constexpr int CB_BYTES = KPS * 128;           // one column box of a stage
+  static constexpr int STAGE_BYTES = 2 * NCB * CB_BYTES;  // K boxes then V boxes
+  static constexpr int STAGES = (HD == 512) ? 3 : 6;   // depth of the shared-memory ring
+  static constexpr int OSTRIDE = DPW + 4;              // floats per head row of a merge slot
+  static constexpr int OSLOT = kGroup * OSTRIDE + 2 * kGroup;  // o[8][DPW+4] | m[8] | l[8]
+  static constexpr int NSLOT = (NKG / 2) * NDQ;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NSLOT * OSLOT * 4 +
+                                 STAGES * sizeof(StageMeta) + 2 * STAGES * 8 + 64;
+  static_assert(NKG >= 2 && NKG * NDQ == kWarps && NT % 2 == 0, "tile shape");
+  static_assert(CB_BYTES % 1024 == 0, "swizzle atoms");
+  static_assert(SMEM <= 232448, "shared memory");
 };
 
-// Number of stages of a problem.
+// Stages of a problem: KPS-aligned blocks of positions covering [lo, hi).
 template <int KPS>
 __device__ __forceinline__ int stages_of(const DecodeParams& p, int prob) {
   uint32_t lo, hi;
   key_range(p, prob / p.nkh, lo, hi);
-  return (int)((hi - lo + KPS - 1) / KPS);
+  return hi > lo ? (int)((hi + KPS - 1) / KPS - lo / KPS) : 0;
 }
 
-// Fixed-width loads of DPL halves from shared memory.
-template <int DPL>
-struct HalfVec;
-template <>
-struct HalfVec<4> {
-  uint32_t w[2];
-  __device__ __forceinline__ void load(const __half* s) {
-    uint2 t = *reinterpret_cast<const uint2*>(s);
-    w[0] = t.x;
-    w[1] = t.y;
-  }
-};
-template <>
-struct HalfVec<8> {
-  uint32_t w[4];
-  __device__ __forceinline__ void load(const __half* s) {
-    uint4 t = *reinterpret_cast<const uint4*>(s);
-    w[0] = t.x;
-    w[1] = t.y;
-    w[2] = t.z;
-    w[3] = t.w;
-  }
-};
-template <>
-struct HalfVec<16> {
-  uint32_t w[8];
-  __device__ __forceinline__ void load(const __half* s) {
-    uint4 t = *reinterpret_cast<const uint4*>(s);
-    uint4 u = *reinterpret_cast<const uint4*>(s + 8);
-    w[0] = t.x;
-    w[1] = t.y;
-    w[2] = t.z;
-    w[3] = t.w;
-    w[4] = u.x;
-    w[5] = u.y;
-    w[6] = u.z;
-    w[7] = u.w;
-  }
-};
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D += A(16x16, f16, row) * B(16x8, f16, col), f32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Pack two floats as f16 (low half = a) and return the residuals x - f32(f16(x)).
+__device__ __forceinline__ uint32_t pack_hi(float a, float b, float& ra, float& rb) {
+  const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+  ra = a - __half2float(ha);
+  rb = b - __half2float(hb);
+  return (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+}
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+// Tiled TMA loads (no multicast) completing on an mbarrier, with an L2 cache hint.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(g4a::smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(g4a::smem_u32(bar)), "l"(pol)
+      : "memory");
+}
 
+// Split-KV flash-decode on the tensor cores.
+//
+// The q block of one kv head (8 heads x HD, f32) is split as q = hi + lo with hi = f16(q) and
+// lo = f16(q - hi) and stacked into the 16 rows of the MMA's A operand (rows 0-7 hi, 8-15 lo),
+// so one m16n8k16 MMA per k-step yields both halves of every score and their sum carries ~22
+// mantissa bits of q; K and V are exact f16.  The probabilities are split the same way for the
+// p*V MMA.  Thread (g = lane/4, c = lane%4) of a warp owns head g: it holds the scores of keys
+// {2c, 2c+1, 8+2c, 9+2c} of its 16-key group (the accumulator rows g and g+8 are the hi and lo
+// halves of the same head), so the online softmax, the hi/lo split of p into the A fragment of
+// the p*V MMA, the masking of out-of-range keys (their scores become -inf and their V halves in
+// the B fragments become 0) and the rescaling of its output accumulators are all thread-local;
+// only the row max and the final row sum need two shuffles.
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_splitkv_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
+                          const __grid_constant__ CUtensorMap tmv) {
   using C = Cfg<HD>;
-  constexpr int HPW = C::HPW, NKW = C::NKW, KPS = C::KPS, DPL = C::DPL, NV = C::NV, DUP = C::DUP;
-  constexpr int ROW = C::ROW_BYTES;
+  constexpr int NDQ = C::NDQ, KPS = C::KPS, KSTEPS = C::KSTEPS, NCB = C::NCB, CBB = C::CB_BYTES;
+  constexpr int NKG = C::NKG, NT = C::NT, DPW = C::DPW, kStages = C::STAGES;
 
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                         ~uintptr_t(1023));
   unsigned char* stage_base = smem;
-  float* obuf = reinterpret_cast<float*>(smem + (size_t)kStages * 2 * C::STAGE_BYTES);
-  float* mlbuf = obuf + C::OBUF_FLOATS;     // [warp][HPW][2]
-  float* pbuf = mlbuf + kWarps * HPW * 2;   // [warp][NV + HPW]
-  StageMeta* meta = reinterpret_cast<StageMeta*>(pbuf + kWarps * (NV + HPW));
+  float* oslot = reinterpret_cast<float*>(smem + (size_t)kStages * C::STAGE_BYTES);
+  StageMeta* meta = reinterpret_cast<StageMeta*>(oslot + C::NSLOT * C::OSLOT);
   uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(meta + kStages) + 7) & ~uintptr_t(7));
   uint64_t* empty = full + kStages;
 
@@ -195,6 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
       g4a::mbar_init(&empty[s], kWarps);
     }
     g4a::fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
   __syncthreads();
 
@@ -222,7 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
   // =========================== producer role (warp 0 issues the TMA copies)
   // Stage n of this CTA goes to slot n % kStages.  Warp 0 keeps the cursor (problem, stage
   // within problem) and, before consuming stage it, issues stage it + kStages - 1 once all
-  // eight warps have released that slot.
+  // eight warps have released that slot.  A stage is the KPS-aligned block of positions
+  // [key0, key0 + KPS); its valid rows are [kfirst, kend).  Rows outside come from the fill of
+  // out-of-range boxes or from neighbouring cache rows and are masked by the consumers.
   int prob = 0, j = 0, nprob = 0;
   uint32_t lo = 0, hi = 0;
   uint64_t pol = 0;
@@ -259,27 +297,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
     if (lane == 0) g4a::mbar_wait_bounded(&empty[slot], par, p.err, G4A_DEVERR_WAIT_EMPTY);
     __syncwarp();
     const int seq = prob / p.nkh, kvh = prob % p.nkh;
-    const uint32_t key0 = lo + (uint32_t)j * KPS;
-    const int nvalid = (int)min((uint32_t)KPS, hi - key0);
-    const __half* krow = nullptr;
-    bool ok = false;
-    if (lane < nvalid) {
-      krow = row_ptr(p, p.k, seq, kvh, key0 + lane);
-      ok = krow != nullptr;
+    const uint32_t key0 = (lo / KPS + (uint32_t)j) * KPS;
+    const int kfirst = (int)(max(lo, key0) - key0);
+    const int kend = (int)(min(hi, key0 + KPS) - key0);
+    const uint32_t sK = g4a::smem_u32(stage_base + (size_t)slot * C::STAGE_BYTES);
+    const uint32_t sV = sK + NCB * CBB;
+    // Sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller than a stage).
+    const int BR = p.page_table ? min(p.page_size, KPS) : KPS;
+    const int nsub = KPS / BR;
+    // Sub-box s is loaded if it holds a valid row and (paged) its page id is in range.
+    bool need = false;
+    if (lane < nsub) {
+      const int r0 = lane * BR;
+      need = (r0 < kend) && (r0 + BR > kfirst);
+      if (need && p.page_table) {
+        const uint32_t pos = key0 + (uint32_t)r0;
+        const uint32_t pidx = pos / (uint32_t)p.page_size;
+        const int my_page = (pidx < (uint32_t)p.max_pages) ? p.page_table[(size_t)seq * p.max_pages + pidx] : -1;
+        if (my_page < 0 || my_page >= p.num_pages) {
+          if (p.err) atomicExch(p.err, G4A_DEVERR_PAGE);
+          need = false;
+        }
+      }
     }
-    // A bad page id skips the row (its keys then read stale shared memory; the error is
-    // reported through g4a_sync).
-    const unsigned okmask = __ballot_sync(0xffffffffu, ok);
-    if (lane < nvalid && !ok && p.err) atomicExch(p.err, G4A_DEVERR_PAGE);
-    const unsigned long long prev = __shfl_up_sync(0xffffffffu, (unsigned long long)(uintptr_t)krow, 1);
-    const bool start =
-        ok && (lane == 0 || !((okmask >> (lane - 1)) & 1u) || (uintptr_t)krow != (uintptr_t)prev + ROW);
-    const unsigned starts = __ballot_sync(0xffffffffu, start);
+    const unsigned need_mask = __ballot_sync(0xffffffffu, need);
     if (lane == 0) {
       StageMeta& mt = meta[slot];
       mt.problem = prob;
       mt.key0 = (int)key0;
-      mt.nvalid = nvalid;
+      mt.kfirst = kfirst;
+      mt.kend = kend;
       int fl = 0;
       if (n == 0 || j == 0) fl |= F_SEG_FIRST;
       if (n == my_stages - 1 || j == nprob - 1) fl |= F_SEG_LAST;
@@ -287,21 +334,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
       if (j == nprob - 1) fl |= F_PROB_LAST;
       mt.flags = fl;
       mt.seg = (int)blockIdx.x + prob;
-      g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)__popc(okmask) * ROW * 2u);
+      g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)__popc(need_mask) * (uint32_t)(BR * 128 * NCB * 2));
     }
     __syncwarp();
-    if (start) {
-      // This lane's run covers lanes [lane, next run start or first skipped lane).
-      const unsigned above = (lane == 31) ? 0u : (0xffffffffu << (lane + 1));
-      const unsigned stop = (starts & above) | (~okmask & above);
-      int end = stop ? (__ffs(stop) - 1) : 32;
-      end = min(end, nvalid);
-      const uint32_t bytes = (uint32_t)(end - lane) * ROW;
-      unsigned char* sK = stage_base + (size_t)slot * 2 * C::STAGE_BYTES + (size_t)lane * ROW;
-      unsigned char* sV = sK + C::STAGE_BYTES;
-      const __half* vrow = p.v + (krow - p.k);
-      g4a::bulk_g2s_hint(sK, krow, bytes, &full[slot], pol);
-      g4a::bulk_g2s_hint(sV, vrow, bytes, &full[slot], pol);
+    // One op per (sub-box, column box, tensor), spread over the lanes.
+    const int nops = nsub * NCB * 2;
+    for (int op = lane; op < nops; op += 32) {
+      const int s = op / (NCB * 2);
+      if (!((need_mask >> s) & 1u)) continue;
+      const int rem = op % (NCB * 2);
+      const int cb = rem >> 1;
+      const bool is_v = rem & 1;
+      const uint32_t dst = (is_v ? sV : sK) + cb * CBB + s * BR * 128;
+      const CUtensorMap* map = is_v ? &tmv : &tmk;
+      if (p.page_table) {
+        // page id of sub-box s (lane s validated it above; the table line is in L1)
+        const uint32_t pos = key0 + (uint32_t)(s * BR);
+        const int page = p.page_table[(size_t)seq * p.max_pages + pos / (uint32_t)p.page_size];
+        tma_load_4d(dst, map, cb * 64, kvh, (int)(pos % (uint32_t)p.page_size), page, &full[slot], pol);
+      } else {
+        const int row = (int)key0 - (int)p.row_base;
+        tma_load_3d(dst, map, cb * 64, kvh, row, &full[slot], pol);
+      }
     }
     if (++j == nprob) {  // advance the cursor to the next problem with stages
       j = 0;
@@ -319,19 +373,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
   }
 
   // =========================== consumer role (all warps)
-  const int hg = warp / NKW;  // head group
-  const int kw = warp % NKW;  // key slot group
-  float2 q2[HPW][DPL / 2];
-  float2 o2[HPW][DPL / 2];
-  float m_run = -INFINITY;  // running max (base 2) of this lane's head
-  float l_part = 0.0f;      // this lane's share of the running sum
+  const int kg = warp / NDQ;  // key group: keys [16 kg, 16 kg + 16) of every stage
+  const int dq = warp % NDQ;  // output dims [DPW dq, DPW dq + DPW)
+  const int g = lane >> 2;    // head owned by this thread
+  const int c = lane & 3;
+  uint32_t qa[KSTEPS][4];     // A fragments of [q_hi; q_lo]
+  float o[NT][4];             // NT n-tiles of 8 output dims: rows g (hi part) and g+8 (lo part)
+  float m_run = -INFINITY;    // running max of head g (base 2)
+  float l_part = 0.f;         // this thread's share of the running sum of head g
   bool seg_whole_start = false;
-
-  // This lane's reduced score slot.
-  const int c_lane = lane / DUP;
-  const int h_lane = c_lane / kG;
-  const int g_lane = c_lane % kG;
-  float* pw = pbuf + warp * (NV + HPW);
+  // ldmatrix lanes: matrix mi = lane/8, row r8 = lane%8.  In a swizzled box, 16-byte chunk ch of
+  // row r sits at chunk ch ^ (r & 7); every row below is a multiple of 8 plus r8.
+  const int mi = lane >> 3, r8 = lane & 7;
+  // K (non-trans): matrices (keys 0-7 | 8-15) x (dims +0 | +8) of a 16-dim k-step.
+  const uint32_t k_row = (uint32_t)(kg * 16 + r8 + 8 * (mi >> 1)) * 128;
+  const int k_chunk = (mi & 1) ^ r8;  // chunk of k-step 0; k-step ks adds 2*(ks&3) by XOR
+  // V (trans): matrices (keys 0-7 | 8-15) x (dims +0 | +8) of a 16-dim pair of n-tiles.
+  const uint32_t v_row = (uint32_t)(kg * 16 + r8 + 8 * (mi & 1)) * 128;
+  const int v_chunk = (mi >> 1) ^ r8;
 
   for (int it = 0; it < my_stages; it++) {
     if (warp == 0 && it + kStages - 1 < my_stages) issue(it + kStages - 1);
@@ -341,251 +400,250 @@ __global__ void __launch_bounds__(kThreads, 1) decode_splitkv_kernel(const Decod
     const StageMeta mt = meta[slot];
 
     if (mt.flags & F_SEG_FIRST) {
-      const float* qp = p.q + ((size_t)mt.problem * kGroup + hg * HPW) * HD + lane * DPL;
+      const float* qp = p.q + ((size_t)mt.problem * kGroup + g) * HD + 2 * c;
 #pragma unroll
-      for (int h = 0; h < HPW; h++) {
-#pragma unroll
-        for (int j4 = 0; j4 < DPL / 4; j4++) {
-          float4 t = *reinterpret_cast<const float4*>(qp + (size_t)h * HD + j4 * 4);
-          q2[h][j4 * 2] = make_float2(t.x, t.y);
-          q2[h][j4 * 2 + 1] = make_float2(t.z, t.w);
-        }
-#pragma unroll
-        for (int jj = 0; jj < DPL / 2; jj++) o2[h][jj] = make_float2(0.f, 0.f);
+      for (int ks = 0; ks < KSTEPS; ks++) {
+        const float2 x0 = *reinterpret_cast<const float2*>(qp + ks * 16);
+        const float2 x1 = *reinterpret_cast<const float2*>(qp + ks * 16 + 8);
+        float r0, r1, r2, r3;
+        qa[ks][0] = pack_hi(x0.x, x0.y, r0, r1);
+        qa[ks][1] = pack_f16(r0, r1);
+        qa[ks][2] = pack_hi(x1.x, x1.y, r2, r3);
+        qa[ks][3] = pack_f16(r2, r3);
       }
+#pragma unroll
+      for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
       m_run = -INFINITY;
-      l_part = 0.0f;
+      l_part = 0.f;
       seg_whole_start = (mt.flags & F_PROB_FIRST) != 0;
     }
 
-    const unsigned char* sK = stage_base + (size_t)slot * 2 * C::STAGE_BYTES;
-    const unsigned char* sV = sK + C::STAGE_BYTES;
-
-    // ---- scores: part[h*G + g] = q_h . k_g over this lane's DPL dims
-    float part[NV];
+    const int kb = kg * 16;
+    if (kb < mt.kend && kb + 16 > mt.kfirst) {  // warp-uniform: the key group has a valid key
+      const uint32_t sK = g4a::smem_u32(stage_base + (size_t)slot * C::STAGE_BYTES);
+      const uint32_t sV = sK + NCB * CBB;
+      // ---- scores of 16 keys: two n-tiles, KSTEPS k-steps (even/odd k-steps in separate
+      // accumulators to halve the MMA dependency chain)
+      float sa0[4] = {0.f, 0.f, 0.f, 0.f}, sa1[4] = {0.f, 0.f, 0.f, 0.f};
+      float sb0[4] = {0.f, 0.f, 0.f, 0.f}, sb1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      const int kl = kw * kG + g;
-      if (kl < mt.nvalid) {
-        HalfVec<DPL> kv;
-        kv.load(reinterpret_cast<const __half*>(sK + (size_t)kl * ROW) + lane * DPL);
-        float2 kf[DPL / 2];
-#pragma unroll
-        for (int jj = 0; jj < DPL / 2; jj++) kf[jj] = g4a::h2_to_f2(kv.w[jj]);
-#pragma unroll
-        for (int h = 0; h < HPW; h++) {
-          float2 acc = __fmul2_rn(q2[h][0], kf[0]);
-#pragma unroll
-          for (int jj = 1; jj < DPL / 2; jj++) acc = __ffma2_rn(q2[h][jj], kf[jj], acc);
-          part[h * kG + g] = acc.x + acc.y;
-        }
-      } else {
-#pragma unroll
-        for (int h = 0; h < HPW; h++) part[h * kG + g] = 0.0f;
+      for (int ks = 0; ks < KSTEPS; ks += 2) {
+        uint32_t b00, b01, b10, b11, c00, c01, c10, c11;
+        const uint32_t box = sK + (ks >> 2) * CBB + k_row;
+        ldsm_x4(box + ((k_chunk ^ (2 * (ks & 3))) << 4), b00, b01, b10, b11);
+        ldsm_x4(box + ((k_chunk ^ (2 * ((ks + 1) & 3))) << 4), c00, c01, c10, c11);
+        mma_16816(sa0, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b00, b01);
+        mma_16816(sa1, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b10, b11);
+        mma_16816(sb0, qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], c00, c01);
+        mma_16816(sb1, qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], c10, c11);
       }
-    }
-    // ---- transposing butterfly: lane ends with the full dot of slot c_lane
+      // keys 2c, 2c+1 (tile 0) and 8+2c, 9+2c (tile 1) of head g: hi row + lo row
+      float t[4] = {sa0[0] + sa0[2] + sb0[0] + sb0[2], sa0[1] + sa0[3] + sb0[1] + sb0[3],
+                    sa1[0] + sa1[2] + sb1[0] + sb1[2], sa1[1] + sa1[3] + sb1[1] + sb1[3]};
+      const int kl[4] = {kb + 2 * c, kb + 2 * c + 1, kb + 8 + 2 * c, kb + 9 + 2 * c};
+      bool ok[4];
+      float mx = -INFINITY;
 #pragma unroll
-    for (int n = NV, mask = 16; n >= 2; n >>= 1, mask >>= 1) {
-      const bool upper = (lane & mask) != 0;
-#pragma unroll
-      for (int jj = 0; jj < n / 2; jj++) {
-        const float keep = upper ? part[jj + n / 2] : part[jj];
-        const float send = upper ? part[jj] : part[jj + n / 2];
-        part[jj] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+      for (int i = 0; i < 4; i++) {
+        ok[i] = kl[i] >= mt.kfirst && kl[i] < mt.kend;
+        t[i] = ok[i] ? t[i] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, t[i]);
       }
-    }
-    float s = part[0];
-    if (DUP == 2) s += __shfl_xor_sync(0xffffffffu, s, 1);
-
-    // ---- online softmax (base 2, lazy rescale)
-    const bool valid = (kw * kG + g_lane) < mt.nvalid;
-    const float t = valid ? s * p.scale_log2 : -INFINITY;
-    float mx = t;
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const bool need = mx > m_run + kLazyRescale;
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ((m_run == -INFINITY) ? 0.f : g4a::fast_exp2(m_run - mx)) : 1.f;
+        if (need) m_run = mx;
+        l_part *= alpha;
 #pragma unroll
-    for (int o = DUP; o < DUP * kG; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const bool need = mx > m_run + kLazyRescale;
-    if (__any_sync(0xffffffffu, need)) {
-      const float m_new = need ? mx : m_run;
-      const float alpha = (need && m_run != -INFINITY) ? g4a::fast_exp2(m_run - m_new) : (need ? 0.0f : 1.0f);
-      m_run = m_new;
-      l_part *= alpha;
-      if (g_lane == 0) pw[NV + h_lane] = alpha;
-      __syncwarp();
-#pragma unroll
-      for (int h = 0; h < HPW; h++) {
-        const float a = pw[NV + h];
-        const float2 a2 = make_float2(a, a);
-#pragma unroll
-        for (int jj = 0; jj < DPL / 2; jj++) o2[h][jj] = __fmul2_rn(o2[h][jj], a2);
+        for (int n = 0; n < NT; n++) {
+          o[n][0] *= alpha;
+          o[n][1] *= alpha;
+          o[n][2] *= alpha;
+          o[n][3] *= alpha;
+        }
       }
-    }
-    const float pr = valid ? g4a::fast_exp2(t - m_run) : 0.0f;
-    l_part += (lane % DUP == 0) ? pr : 0.0f;
-    pw[g_lane * HPW + h_lane] = pr;
-    __syncwarp();
-
-    // ---- o += p * V
+      float pr[4];
 #pragma unroll
-    for (int g = 0; g < kG; g++) {
-      const int kl = kw * kG + g;
-      if (kl < mt.nvalid) {
-        HalfVec<DPL> vv;
-        vv.load(reinterpret_cast<const __half*>(sV + (size_t)kl * ROW) + lane * DPL);
-        float pg[HPW];
+      for (int i = 0; i < 4; i++) {
+        pr[i] = ok[i] ? g4a::fast_exp2(t[i] - m_run) : 0.f;
+        l_part += pr[i];
+      }
+      float e0, e1, e2, e3;
+      const uint32_t pa0 = pack_hi(pr[0], pr[1], e0, e1);
+      const uint32_t pa1 = pack_f16(e0, e1);
+      const uint32_t pa2 = pack_hi(pr[2], pr[3], e2, e3);
+      const uint32_t pa3 = pack_f16(e2, e3);
+      // ---- o += p * V over this warp's DPW output dims (NT/2 pairs of n-tiles).  The B
+      // fragment halves of this thread belong to its own keys {2c, 2c+1} (b*0) and {8+2c, 9+2c}
+      // (b*1); halves of keys outside the stage's valid range are zeroed.
+      const uint32_t mlo = (ok[0] ? 0x0000ffffu : 0u) | (ok[1] ? 0xffff0000u : 0u);
+      const uint32_t mhi = (ok[2] ? 0x0000ffffu : 0u) | (ok[3] ? 0xffff0000u : 0u);
 #pragma unroll
-        for (int h4 = 0; h4 < HPW / 4; h4++) {
-          const float4 t4 = *reinterpret_cast<const float4*>(pw + g * HPW + h4 * 4);
-          pg[h4 * 4 + 0] = t4.x;
-          pg[h4 * 4 + 1] = t4.y;
-          pg[h4 * 4 + 2] = t4.z;
-          pg[h4 * 4 + 3] = t4.w;
-        }
-        float2 vf[DPL / 2];
-#pragma unroll
-        for (int jj = 0; jj < DPL / 2; jj++) vf[jj] = g4a::h2_to_f2(vv.w[jj]);
-#pragma unroll
-        for (int h = 0; h < HPW; h++) {
-          const float2 p2 = make_float2(pg[h], pg[h]);
-#pragma unroll
-          for (int jj = 0; jj < DPL / 2; jj++) o2[h][jj] = __ffma2_rn(p2, vf[jj], o2[h][jj]);
-        }
+      for (int np = 0; np < NT / 2; np++) {
+        const int dim = dq * DPW + np * 16;  // first dim of the pair of n-tiles
+        const uint32_t box = sV + (dim >> 6) * CBB + v_row;
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_trans(box + ((v_chunk ^ ((dim & 63) >> 3)) << 4), b00, b01, b10, b11);
+        mma_16816(o[2 * np], pa0, pa1, pa2, pa3, b00 & mlo, b01 & mhi);
+        mma_16816(o[2 * np + 1], pa0, pa1, pa2, pa3, b10 & mlo, b11 & mhi);
       }
     }
     __syncwarp();
     if (lane == 0) g4a::mbar_arrive(&empty[slot]);
 
     if (mt.flags & F_SEG_LAST) {
-      // ---- merge the 8 warps of this CTA for this segment
+      // ---- merge the NKG key groups of each output slice (tree over shared memory)
       float l_head = l_part;
+      l_head += __shfl_xor_sync(0xffffffffu, l_head, 1);
+      l_head += __shfl_xor_sync(0xffffffffu, l_head, 2);
+      float ov[NT][2];
 #pragma unroll
-      for (int o = DUP; o < DUP * kG; o <<= 1) l_head += __shfl_xor_sync(0xffffffffu, l_head, o);
-      if (g_lane == 0 && (lane % DUP) == 0) {
-        mlbuf[(warp * HPW + h_lane) * 2 + 0] = m_run;
-        mlbuf[(warp * HPW + h_lane) * 2 + 1] = l_head;
+      for (int n = 0; n < NT; n++) {
+        ov[n][0] = o[n][0] + o[n][2];
+        ov[n][1] = o[n][1] + o[n][3];
       }
-      float* ow = obuf + (size_t)warp * HPW * HD;
+      float m_h = m_run;
 #pragma unroll
-      for (int h = 0; h < HPW; h++) {
+      for (int stride = NKG / 2; stride >= 1; stride >>= 1) {
+        if (kg >= stride && kg < 2 * stride) {
+          float* sl = oslot + ((kg - stride) * NDQ + dq) * C::OSLOT;
 #pragma unroll
-        for (int j4 = 0; j4 < DPL / 4; j4++) {
-          *reinterpret_cast<float4*>(ow + h * HD + lane * DPL + j4 * 4) =
-              make_float4(o2[h][j4 * 2].x, o2[h][j4 * 2].y, o2[h][j4 * 2 + 1].x, o2[h][j4 * 2 + 1].y);
-        }
-      }
-      g4a::named_bar_sync(1, kThreads);
-      const bool whole = seg_whole_start && (mt.flags & F_PROB_LAST);
-      const int tid = threadIdx.x;
-      float* part_row = p.part + (size_t)mt.seg * (kGroup * (HD + 2));
-      for (int e = tid; e < kGroup * HD; e += kThreads) {
-        const int h8 = e / HD, d = e % HD;
-        const int g0 = h8 / HPW, hh = h8 % HPW;
-        float M = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < NKW; k++) M = fmaxf(M, mlbuf[((g0 * NKW + k) * HPW + hh) * 2]);
-        float acc = 0.f, lsum = 0.f;
-#pragma unroll
-        for (int k = 0; k < NKW; k++) {
-          const int cw = g0 * NKW + k;
-          const float mk = mlbuf[(cw * HPW + hh) * 2];
-          const float sc = (mk == -INFINITY) ? 0.f : g4a::fast_exp2(mk - M);
-          acc += sc * obuf[((size_t)cw * HPW + hh) * HD + d];
-          lsum += sc * mlbuf[(cw * HPW + hh) * 2 + 1];
-        }
-        if (whole && p.out != nullptr) {
-          p.out[((size_t)mt.problem * kGroup + h8) * HD + d] = acc / lsum;
-        } else {
-          part_row[2 * kGroup + h8 * HD + d] = acc;
-          if (d == 0) {
-            part_row[h8] = M;
-            part_row[kGroup + h8] = lsum;
+          for (int n = 0; n < NT; n++)
+            *reinterpret_cast<float2*>(sl + g * C::OSTRIDE + n * 8 + 2 * c) = make_float2(ov[n][0], ov[n][1]);
+          if (c == 0) {
+            sl[kGroup * C::OSTRIDE + g] = m_h;
+            sl[kGroup * C::OSTRIDE + kGroup + g] = l_head;
           }
         }
+        g4a::named_bar_sync(1, kThreads);
+        if (kg < stride) {
+          const float* sl = oslot + (kg * NDQ + dq) * C::OSLOT;
+          const float mb = sl[kGroup * C::OSTRIDE + g];
+          const float lb = sl[kGroup * C::OSTRIDE + kGroup + g];
+          const float M = fmaxf(m_h, mb);
+          const float wa = (m_h == -INFINITY) ? 0.f : g4a::fast_exp2(m_h - M);
+          const float wb = (mb == -INFINITY) ? 0.f : g4a::fast_exp2(mb - M);
+#pragma unroll
+          for (int n = 0; n < NT; n++) {
+            const float2 x = *reinterpret_cast<const float2*>(sl + g * C::OSTRIDE + n * 8 + 2 * c);
+            ov[n][0] = ov[n][0] * wa + x.x * wb;
+            ov[n][1] = ov[n][1] * wa + x.y * wb;
+          }
+          l_head = l_head * wa + lb * wb;
+          m_h = M;
+        }
+        g4a::named_bar_sync(1, kThreads);
       }
-      if (tid == 0) {
-        if (seg_whole_start) p.seg_range[mt.problem].x = mt.seg;
-        if (mt.flags & F_PROB_LAST) p.seg_range[mt.problem].y = mt.seg;
+      if (kg == 0) {
+        const bool whole = seg_whole_start && (mt.flags & F_PROB_LAST);
+        if (whole && p.out != nullptr) {
+          const float inv = 1.0f / l_head;
+          float* op = p.out + ((size_t)mt.problem * kGroup + g) * HD + dq * DPW + 2 * c;
+#pragma unroll
+          for (int n = 0; n < NT; n++)
+            *reinterpret_cast<float2*>(op + n * 8) = make_float2(ov[n][0] * inv, ov[n][1] * inv);
+        } else {
+          float* part_row = p.part + (size_t)mt.seg * (kGroup * (HD + 2));
+          float* op = part_row + 2 * kGroup + g * HD + dq * DPW + 2 * c;
+#pragma unroll
+          for (int n = 0; n < NT; n++) *reinterpret_cast<float2*>(op + n * 8) = make_float2(ov[n][0], ov[n][1]);
+          if (dq == 0 && c == 0) {
+            part_row[g] = m_h;
+            part_row[kGroup + g] = l_head;
+          }
+        }
+        if (warp == 0 && lane == 0) {
+          if (seg_whole_start) p.seg_range[mt.problem].x = mt.seg;
+          if (mt.flags & F_PROB_LAST) p.seg_range[mt.problem].y = mt.seg;
+        }
       }
-      g4a::named_bar_sync(1, kThreads);
     }
   }
 }
 
-// Merge the segments of each problem.  grid (P, 8, HD/64), 256 threads: 16 segment lanes x 16
-// float4 columns.  mode 0: normalised output rows; mode 1: one merged partial per problem.
+// Merge the segments of each problem: one CTA per (problem, head, 16 output dims), 16 segment
+// lanes x 16 dims.  Every thread merges its segments with a running log-sum-exp.  mode 0: normalised
+// output rows (problems with a single segment were written by the main kernel); mode 1: one
+// merged partial per problem.
 __global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
   g4a::pdl_wait_primary();
-  const int prob = blockIdx.x, h = blockIdx.y, dchunk = blockIdx.z;
+  const int prob = blockIdx.x, h = blockIdx.y;
   const int hd = p.hd;
-  const int sg = threadIdx.x / 16, c4 = threadIdx.x % 16;
-  const int d = dchunk * 64 + c4 * 4;
+  const int sg = threadIdx.x >> 4, dl = threadIdx.x & 15;
+  const int d = blockIdx.z * 16 + dl;
   const size_t prow = (size_t)kGroup * (hd + 2);
   uint32_t lo, hi;
   key_range(p, prob / p.nkh, lo, hi);
   if (hi <= lo) {  // no visible key: zeros (the reference's seq_len 0 output)
-    if (mode == 0) {
-      if (sg == 0) *reinterpret_cast<float4*>(p.out + ((size_t)prob * kGroup + h) * hd + d) = make_float4(0, 0, 0, 0);
-    } else {
-      float* po = part_out + (size_t)prob * prow;
-      if (sg == 0) *reinterpret_cast<float4*>(po + 2 * kGroup + h * hd + d) = make_float4(0, 0, 0, 0);
-      if (threadIdx.x == 0 && dchunk == 0) {
-        po[h] = -INFINITY;
-        po[kGroup + h] = 0.f;
+    if (sg == 0) {
+      if (mode == 0) {
+        p.out[((size_t)prob * kGroup + h) * hd + d] = 0.f;
+      } else {
+        float* po = part_out + (size_t)prob * prow;
+        po[2 * kGroup + h * hd + d] = 0.f;
+        if (dl == 0 && blockIdx.z == 0) {
+          po[h] = -INFINITY;
+          po[kGroup + h] = 0.f;
+        }
       }
     }
     return;
   }
   const int2 r = p.seg_range[prob];
   if (mode == 0 && r.x == r.y) return;  // single segment: the main kernel wrote the row
-  __shared__ float smax[16];
-  __shared__ float4 sacc[16][16];
-  __shared__ float sl[16];
-  float M = -INFINITY;
-  for (int s = r.x + sg; s <= r.y; s += 16) M = fmaxf(M, p.part[(size_t)s * prow + h]);
-  if (c4 == 0) smax[sg] = M;
-  __syncthreads();
-  M = -INFINITY;
+  // Loads of a batch of 8 segments per thread are issued before any of them is used (clamped
+  // addresses stay inside the range), so a batch costs one memory round trip.
+  float M = -INFINITY, L = 0.f, acc = 0.f;
+  for (int base = r.x + sg; base <= r.y; base += 16 * 8) {
+    float mv[8], lv[8], ov[8];
 #pragma unroll
-  for (int i = 0; i < 16; i++) M = fmaxf(M, smax[i]);
-  float4 acc = make_float4(0, 0, 0, 0);
-  float lsum = 0.f;
-#pragma unroll 4
-  for (int s = r.x + sg; s <= r.y; s += 16) {
-    const float* row = p.part + (size_t)s * prow;
-    const float ms = row[h];
-    if (ms == -INFINITY) continue;  // empty segment: contributes nothing (its o is not read)
-    const float sc = exp2f(ms - M);
-    const float4 o = *reinterpret_cast<const float4*>(row + 2 * kGroup + h * hd + d);
-    acc.x += sc * o.x;
-    acc.y += sc * o.y;
-    acc.z += sc * o.z;
-    acc.w += sc * o.w;
-    lsum += sc * row[kGroup + h];
+    for (int i = 0; i < 8; i++) {
+      const int s = base + 16 * i;
+      const float* row = p.part + (size_t)(s <= r.y ? s : r.x) * prow;
+      mv[i] = row[h];
+      lv[i] = row[kGroup + h];
+      ov[i] = row[2 * kGroup + (size_t)h * hd + d];
+      if (s > r.y) mv[i] = -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (mv[i] == -INFINITY) continue;
+      const float Mn = fmaxf(M, mv[i]);
+      const float wa = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+      const float wb = exp2f(mv[i] - Mn);
+      acc = acc * wa + ov[i] * wb;
+      L = L * wa + lv[i] * wb;
+      M = Mn;
+    }
   }
-  sacc[sg][c4] = acc;
-  if (c4 == 0) sl[sg] = lsum;
+  __shared__ float sM[16][16], sL[16][16], sA[16][16];
+  sM[sg][dl] = M;
+  sL[sg][dl] = L;
+  sA[sg][dl] = acc;
   __syncthreads();
   if (sg == 0) {
-    float4 a = make_float4(0, 0, 0, 0);
-    float L = 0.f;
+    float Mt = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; i++) Mt = fmaxf(Mt, sM[i][dl]);
+    float Lt = 0.f, At = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; i++) {
-      a.x += sacc[i][c4].x;
-      a.y += sacc[i][c4].y;
-      a.z += sacc[i][c4].z;
-      a.w += sacc[i][c4].w;
-      L += sl[i];
+      const float mi = sM[i][dl];
+      if (mi == -INFINITY) continue;
+      const float w = exp2f(mi - Mt);
+      Lt += sL[i][dl] * w;
+      At += sA[i][dl] * w;
     }
     if (mode == 0) {
-      const float inv = 1.0f / L;
-      *reinterpret_cast<float4*>(p.out + ((size_t)prob * kGroup + h) * hd + d) =
-          make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+      p.out[((size_t)prob * kGroup + h) * hd + d] = At / Lt;
     } else {
       float* po = part_out + (size_t)prob * prow;
-      *reinterpret_cast<float4*>(po + 2 * kGroup + h * hd + d) = a;
-      if (c4 == 0 && dchunk == 0) {
-        po[h] = M;
-        po[kGroup + h] = L;
+      po[2 * kGroup + h * hd + d] = At;
+      if (dl == 0 && blockIdx.z == 0) {
+        po[h] = Mt;
+        po[kGroup + h] = Lt;
       }
     }
   }
@@ -699,6 +757,14 @@ bool fast_path_ok(uint32_t nqh, uint32_t nkh, uint32_t hd) {
   return nkh > 0 && nqh == kGroup * nkh && (hd == 128 || hd == 256 || hd == 512);
 }
 
+int kps_of(uint32_t hd);
+
+// The paged fast path loads page-aligned boxes: pages must tile stages (or stages pages).
+bool paged_fast_ok(uint32_t page_size, uint32_t hd) {
+  const uint32_t kps = (uint32_t)kps_of(hd);
+  return page_size >= 8 && page_size <= 256 * 1024 && (page_size % kps == 0 || kps % page_size == 0);
+}
+
 template <int HD>
 g4a_status configure_kernel(g4a_ctx* ctx) {
   static bool done[64] = {false};
@@ -710,12 +776,57 @@ g4a_status configure_kernel(g4a_ctx* ctx) {
   return G4A_OK;
 }
 
+// Resolve cuTensorMapEncodeTiled from the driver once per context (no link-time libcuda).
+g4a_status get_encoder(g4a_ctx* ctx, PFN_cuTensorMapEncodeTiled_v12000* out) {
+  if (!ctx->encode_tiled) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    ctx->encode_tiled = fn;
+  }
+  *out = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ctx->encode_tiled);
+  return G4A_OK;
+}
+
+// Tensor maps of the K and V caches: 64-dim x 1-head x KPS-row boxes (or page-sized boxes) with
+// the 128-byte swizzle, zero fill outside the tensor.  Contiguous: [rows, nkh, hd] with rows =
+// the positions held by the buffer.  Paged: [num_pages, page_size, nkh, hd].
+g4a_status encode_kv_maps(g4a_ctx* ctx, const DecodeParams& p, int kps, uint64_t rows, CUtensorMap* mk,
+                          CUtensorMap* mv) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (g4a_status s = get_encoder(ctx, &enc)) return s;
+  const cuuint64_t hd = (cuuint64_t)p.hd, nkh = (cuuint64_t)p.nkh;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
+  cuuint32_t rank;
+  if (p.page_table) {
+    rank = 4;
+    dims[0] = hd; dims[1] = nkh; dims[2] = (cuuint64_t)p.page_size; dims[3] = (cuuint64_t)p.num_pages;
+    strides[0] = hd * 2; strides[1] = nkh * hd * 2; strides[2] = (cuuint64_t)p.page_size * nkh * hd * 2;
+    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)std::min(p.page_size, kps); box[3] = 1;
+  } else {
+    rank = 3;
+    dims[0] = hd; dims[1] = nkh; dims[2] = rows;
+    strides[0] = hd * 2; strides[1] = nkh * hd * 2;
+    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)kps;
+  }
+  for (int t = 0; t < 2; t++) {
+    CUresult r = enc(t ? mv : mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<__half*>(t ? p.v : p.k), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled failed (%d) for the %s cache", (int)r, t ? "V" : "K");
+  }
+  return G4A_OK;
+}
+
 template <int HD>
 g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, int mode, float* part_out, bool pdl) {
   using C = Cfg<HD>;
   if (g4a_status s = configure_kernel<HD>(ctx)) return s;
   const int P = p.B * p.nkh;
-  int grid = (int)std::min<long long>(stages_upper, (long long)ctx->num_sms);
+  int grid = (int)std::min<long long>(stages_upper + P, (long long)ctx->num_sms);
   if (grid < 1) grid = 1;
   const size_t prow = (size_t)kGroup * (HD + 2) * sizeof(float);
   const size_t segs = (size_t)grid + (size_t)P + 1;
@@ -725,8 +836,14 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   p.seg_range = reinterpret_cast<int2*>(reinterpret_cast<char*>(ctx->workspace) + part_bytes);
   p.err = ctx->dev_err_dev;
   if (stages_upper > 0) {
+    // rows held by a contiguous buffer: positions [row_base, min(kv_end, kv_len))
+    const uint64_t end = std::min<uint64_t>(p.kv_end, p.kv_len_scalar);
+    const uint64_t rows = end > p.row_base ? end - p.row_base : 1;
+    CUtensorMap mk, mv;
+    if (g4a_status s = encode_kv_maps(ctx, p, C::KPS, rows, &mk, &mv)) return s;
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_SPLITKV);
-    cudaError_t e = g4a_launch(decode_splitkv_kernel<HD>, dim3(grid), dim3(kThreads), C::SMEM, ctx->stream, pdl, p);
+    cudaError_t e =
+        g4a_launch(decode_splitkv_kernel<HD>, dim3(grid), dim3(kThreads), C::SMEM, ctx->stream, pdl, p, mk, mv);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch decode_splitkv_kernel");
   }
   // The merge kernel is needed when a problem can span several CTAs, for zero-length problems,
@@ -734,7 +851,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   const bool need_merge = (mode == 1) || grid > 1 || stages_upper == 0 || P > 1;
   if (need_merge) {
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_MERGE);
-    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 64), dim3(256), 0, ctx->stream,
+    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 16), dim3(256), 0, ctx->stream,
                                stages_upper > 0, p, mode, part_out);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch merge_segments_kernel");
   }
@@ -755,7 +872,7 @@ g4a_status dispatch_fast(g4a_ctx* ctx, DecodeParams& p, long long keys_upper, in
   }
 }
 
-int kps_of(uint32_t hd) { return hd == 512 ? Cfg<512>::KPS : Cfg<256>::KPS; }
+int kps_of(uint32_t hd) { return hd == 512 ? Cfg<512>::KPS : hd == 256 ? Cfg<256>::KPS : Cfg<128>::KPS; }
 
 g4a_status check_common(const char* fn, const void* q, const void* k, const void* v, const void* out, uint32_t nqh,
                         uint32_t nkh, uint32_t hd) {
@@ -842,7 +959,7 @@ g4a_status g4a_decode_attn_paged(g4a_ctx* ctx, const float* q, const uint16_t* k
   p.max_pages = (int)max_pages_per_seq;
   p.num_pages = (int)num_pages;
   p.err = ctx->dev_err_dev;
-  if (fast_path_ok(num_q_heads, num_kv_heads, head_dim)) {
+  if (fast_path_ok(num_q_heads, num_kv_heads, head_dim) && paged_fast_ok(page_size, head_dim)) {
     long long keys = 0;
     const uint64_t cap = (uint64_t)page_size * max_pages_per_seq;
     for (uint32_t b = 0; b < batch; b++) {

@@ -31,7 +31,7 @@ def _paged_setup(ctx, oracle, lengths, page_size, theta, seed, hd=256):
     return np.stack(qs), kp, vp, table, caches
 
 
-@pytest.mark.parametrize("page_size", [64, 16, 128])
+@pytest.mark.parametrize("page_size", [64, 16, 128, 8, 48])
 @pytest.mark.parametrize("W", [0, 512])
 def test_paged_batch_matches_oracle(ctx, oracle, page_size, W):
     rng = np.random.default_rng(page_size + W)
@@ -90,9 +90,9 @@ def test_bad_page_id_is_reported_not_read(ctx, oracle):
     assert_attention_close(host(out)[1], ref, what="healthy sequence next to a bad one")
 
 
-@pytest.mark.parametrize("n", [1, 2, 3, 8])
+@pytest.mark.parametrize("n,align", [(1, 32), (2, 32), (3, 32), (8, 32), (3, 1), (5, 7)])
 @pytest.mark.parametrize("L,W", [(5000, 0), (2000, 512), (100000, 0)])
-def test_splitkv_partials_merge(ctx, oracle, n, L, W):
+def test_splitkv_partials_merge(ctx, oracle, n, align, L, W):
     """Emulates n ranks on one GPU: each slice's partial over its own buffer, then the merge."""
     raw = synth.raw_layer(7, L, hd=256, theta=1e6)
     kc, vc = gpu_build_cache(ctx, raw.k, raw.v, raw.k_w, theta=1e6)
@@ -100,7 +100,7 @@ def test_splitkv_partials_merge(ctx, oracle, n, L, W):
     qd = dev(q)
     pf = dist.partial_floats(8, 256)
     parts = torch.zeros((n, pf), device="cuda")
-    for r, (b, e) in enumerate(dist.splitkv_ranges(L, n)):
+    for r, (b, e) in enumerate(dist.splitkv_ranges(L, n, align)):
         ks = kc[b:e].contiguous()
         vs = vc[b:e].contiguous()
         ctx.decode_attn_partial(qd, ks, vs, parts[r], num_q_heads=8, num_kv_heads=1, head_dim=256, kv_begin=b,
@@ -115,7 +115,7 @@ def test_splitkv_partials_merge(ctx, oracle, n, L, W):
     assert_attention_close(dist.merge_partials_host(host(parts), 8, 256), ref, what="host merge")
     # partial semantics: l * 2^m equals the oracle's sum of exp over the slice
     ph = host(parts)
-    for r, (b, e) in enumerate(dist.splitkv_ranges(L, n)):
+    for r, (b, e) in enumerate(dist.splitkv_ranges(L, n, align)):
         m, l_, o = oracle.decode_partial_f64(q, host(kc), host(vc), num_q_heads=8, num_kv_heads=1, head_dim=256,
                                              kv_begin=b, kv_end=e, kv_len=L, sliding_window=W)
         mg, lg = ph[r, :8].astype(np.float64), ph[r, 8:16].astype(np.float64)
