@@ -353,10 +353,13 @@ def run_ours(args):
     us_per_layer = ms_per_step * 1e3 / R
     hbm, _, peak_kind = peaks()
 
-    # ---- kernel-level roofline: same steps with the per-kernel profiler (events per launch)
+    # ---- kernel-level roofline: same steps with the per-kernel profiler (events per launch).
+    # A bounded sleep kernel first lets the host enqueue ahead of the GPU, so the events time
+    # the kernels and not the host's launch latency.
     ctx.profile_reset()
     ctx.profile_enable(True)
-    n_prof = max(1, min(args.steps, 64))
+    n_prof = max(1, min(args.steps, 32))
+    torch.cuda._sleep(100_000_000)
     for _ in range(n_prof):
         for r in range(R):
             ctx.decode_attn(qs[r], kcs[r], vcs[r], outs[r], num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,

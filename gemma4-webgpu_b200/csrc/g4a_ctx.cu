@@ -210,7 +210,13 @@ g4a_status g4a_destroy(g4a_ctx* ctx) {
 
 g4a_status g4a_set_stream(g4a_ctx* ctx, void* cuda_stream) {
   G4A_CHECK_CTX(ctx);
-  ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own_stream;
+  ctx->stream = (cudaStream_t)cuda_stream;  // 0 is the legacy default stream
+  return G4A_OK;
+}
+
+g4a_status g4a_use_own_stream(g4a_ctx* ctx) {
+  G4A_CHECK_CTX(ctx);
+  ctx->stream = ctx->own_stream;
   return G4A_OK;
 }
 

@@ -107,9 +107,10 @@ __device__ __forceinline__ const __half* row_ptr(const DecodeParams& p, const __
 }
 
 // Tile shape of the tensor-core decode kernel for one head_dim.  The 8 warps of a CTA form NKG
-// key groups of 16 keys x NDQ slices of DPW output dims: every warp computes the scores of its
-// key group (the NDQ warps of a group compute identical scores on the tensor cores, which have
-// throughput to spare) and accumulates p*V for its DPW output dims.  A stage holds KPS keys of
+// key groups of 16 keys x NDQ slices.  Warp (kg, dq) contracts the scores of key group kg over
+// the dq-th slice of HD/NDQ dims; the NDQ partial scores are summed through shared memory (in a
+// fixed order, so every warp of the group holds identical scores), and the warp then
+// accumulates p*V for its DPW output dims.  A stage holds KPS keys of
 // K and of V as HD/64 column boxes of [KPS rows x 128 B] each, written by TMA with the 128-byte
 // swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7)), so ldmatrix reads of 8 rows
 // hit 8 different bank groups without padding.
@@ -121,6 +122,7 @@ struct Cfg {
   static constexpr int NKG = kWarps / NDQ;             // key groups of 16 keys
   static constexpr int KPS = 16 * NKG;                 // keys per stage
   static constexpr int KSTEPS = HD / 16;               // k-steps of the score MMA
+  static constexpr int KPW = KSTEPS / NDQ;             // k-steps of the score MMA per warp
   static constexpr int NCB = HD / 64;                  // 64-dim column boxes per row
   static constexpr int CB_BYTES = KPS * 128;           // one column box of a stage
   static constexpr int STAGE_BYTES = 2 * NCB * CB_BYTES;  // K boxes then V boxes
@@ -128,9 +130,10 @@ struct Cfg {
   static constexpr int OSTRIDE = DPW + 4;              // floats per head row of a merge slot
   static constexpr int OSLOT = kGroup * OSTRIDE + 2 * kGroup;  // o[8][DPW+4] | m[8] | l[8]
   static constexpr int NSLOT = (NKG / 2) * NDQ;
+  static constexpr int SX_FLOATS = 2 * kWarps * 32 * 4;  // double-buffered partial-score exchange
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NSLOT * OSLOT * 4 +
-                                 STAGES * sizeof(StageMeta) + 2 * STAGES * 8 + 64;
-  static_assert(NKG >= 2 && NKG * NDQ == kWarps && NT % 2 == 0, "tile shape");
+                                 (size_t)SX_FLOATS * 4 + STAGES * sizeof(StageMeta) + 2 * STAGES * 8 + 64;
+  static_assert(NKG >= 2 && NKG * NDQ == kWarps && NT % 2 == 0 && KPW % 4 == 0, "tile shape");
   static_assert(CB_BYTES % 1024 == 0, "swizzle atoms");
   static_assert(SMEM <= 232448, "shared memory");
 };
@@ -207,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     decode_splitkv_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
   using C = Cfg<HD>;
-  constexpr int NDQ = C::NDQ, KPS = C::KPS, KSTEPS = C::KSTEPS, NCB = C::NCB, CBB = C::CB_BYTES;
+  constexpr int NDQ = C::NDQ, KPS = C::KPS, KPW = C::KPW, NCB = C::NCB, CBB = C::CB_BYTES;
   constexpr int NKG = C::NKG, NT = C::NT, DPW = C::DPW, kStages = C::STAGES;
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -215,7 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                          ~uintptr_t(1023));
   unsigned char* stage_base = smem;
   float* oslot = reinterpret_cast<float*>(smem + (size_t)kStages * C::STAGE_BYTES);
-  StageMeta* meta = reinterpret_cast<StageMeta*>(oslot + C::NSLOT * C::OSLOT);
+  float* sx = oslot + C::NSLOT * C::OSLOT;  // [2][warp][lane][4] partial scores
+  StageMeta* meta = reinterpret_cast<StageMeta*>(sx + C::SX_FLOATS);
   uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(meta + kStages) + 7) & ~uintptr_t(7));
   uint64_t* empty = full + kStages;
 
@@ -377,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int dq = warp % NDQ;  // output dims [DPW dq, DPW dq + DPW)
   const int g = lane >> 2;    // head owned by this thread
   const int c = lane & 3;
-  uint32_t qa[KSTEPS][4];     // A fragments of [q_hi; q_lo]
+  uint32_t qa[KPW][4];        // A fragments of [q_hi; q_lo] for this warp's k-steps
   float o[NT][4];             // NT n-tiles of 8 output dims: rows g (hi part) and g+8 (lo part)
   float m_run = -INFINITY;    // running max of head g (base 2)
   float l_part = 0.f;         // this thread's share of the running sum of head g
@@ -400,9 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const StageMeta mt = meta[slot];
 
     if (mt.flags & F_SEG_FIRST) {
-      const float* qp = p.q + ((size_t)mt.problem * kGroup + g) * HD + 2 * c;
+      const float* qp = p.q + ((size_t)mt.problem * kGroup + g) * HD + dq * KPW * 16 + 2 * c;
 #pragma unroll
-      for (int ks = 0; ks < KSTEPS; ks++) {
+      for (int ks = 0; ks < KPW; ks++) {
         const float2 x0 = *reinterpret_cast<const float2*>(qp + ks * 16);
         const float2 x1 = *reinterpret_cast<const float2*>(qp + ks * 16 + 8);
         float r0, r1, r2, r3;
@@ -422,24 +426,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kb < mt.kend && kb + 16 > mt.kfirst) {  // warp-uniform: the key group has a valid key
       const uint32_t sK = g4a::smem_u32(stage_base + (size_t)slot * C::STAGE_BYTES);
       const uint32_t sV = sK + NCB * CBB;
-      // ---- scores of 16 keys: two n-tiles, KSTEPS k-steps (even/odd k-steps in separate
-      // accumulators to halve the MMA dependency chain)
+      // ---- partial scores of 16 keys over this warp's KPW k-steps (two n-tiles; even and odd
+      // k-steps in separate accumulators to halve the MMA dependency chain)
       float sa0[4] = {0.f, 0.f, 0.f, 0.f}, sa1[4] = {0.f, 0.f, 0.f, 0.f};
       float sb0[4] = {0.f, 0.f, 0.f, 0.f}, sb1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ks = 0; ks < KSTEPS; ks += 2) {
+      for (int j = 0; j < KPW; j += 2) {
         uint32_t b00, b01, b10, b11, c00, c01, c10, c11;
-        const uint32_t box = sK + (ks >> 2) * CBB + k_row;
-        ldsm_x4(box + ((k_chunk ^ (2 * (ks & 3))) << 4), b00, b01, b10, b11);
-        ldsm_x4(box + ((k_chunk ^ (2 * ((ks + 1) & 3))) << 4), c00, c01, c10, c11);
-        mma_16816(sa0, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b00, b01);
-        mma_16816(sa1, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b10, b11);
-        mma_16816(sb0, qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], c00, c01);
-        mma_16816(sb1, qa[ks + 1][0], qa[ks + 1][1], qa[ks + 1][2], qa[ks + 1][3], c10, c11);
+        const uint32_t box = sK + (dq * (KPW / 4) + (j >> 2)) * CBB + k_row;
+        ldsm_x4(box + ((k_chunk ^ (2 * (j & 3))) << 4), b00, b01, b10, b11);
+        ldsm_x4(box + ((k_chunk ^ (2 * ((j + 1) & 3))) << 4), c00, c01, c10, c11);
+        mma_16816(sa0, qa[j][0], qa[j][1], qa[j][2], qa[j][3], b00, b01);
+        mma_16816(sa1, qa[j][0], qa[j][1], qa[j][2], qa[j][3], b10, b11);
+        mma_16816(sb0, qa[j + 1][0], qa[j + 1][1], qa[j + 1][2], qa[j + 1][3], c00, c01);
+        mma_16816(sb1, qa[j + 1][0], qa[j + 1][1], qa[j + 1][2], qa[j + 1][3], c10, c11);
       }
       // keys 2c, 2c+1 (tile 0) and 8+2c, 9+2c (tile 1) of head g: hi row + lo row
-      float t[4] = {sa0[0] + sa0[2] + sb0[0] + sb0[2], sa0[1] + sa0[3] + sb0[1] + sb0[3],
-                    sa1[0] + sa1[2] + sb1[0] + sb1[2], sa1[1] + sa1[3] + sb1[1] + sb1[3]};
+      float4 mine = make_float4(sa0[0] + sa0[2] + sb0[0] + sb0[2], sa0[1] + sa0[3] + sb0[1] + sb0[3],
+                                sa1[0] + sa1[2] + sb1[0] + sb1[2], sa1[1] + sa1[3] + sb1[1] + sb1[3]);
+      // ---- sum the NDQ partials of this key group (fixed order: identical in every warp)
+      float4* sxb = reinterpret_cast<float4*>(sx) + (size_t)(it & 1) * kWarps * 32;
+      sxb[warp * 32 + lane] = mine;
+      g4a::named_bar_sync(2 + kg, NDQ * 32);
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int d2 = 0; d2 < NDQ; d2++) {
+        const float4 x = sxb[(kg * NDQ + d2) * 32 + lane];
+        t[0] += x.x;
+        t[1] += x.y;
+        t[2] += x.z;
+        t[3] += x.w;
+      }
       const int kl[4] = {kb + 2 * c, kb + 2 * c + 1, kb + 8 + 2 * c, kb + 9 + 2 * c};
       bool ok[4];
       float mx = -INFINITY;
@@ -563,11 +580,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merge the segments of each problem: one CTA per (problem, head, 16 output dims), 16 segment
-// lanes x 16 dims.  Every thread merges its segments with a running log-sum-exp.  mode 0: normalised
-// output rows (problems with a single segment were written by the main kernel); mode 1: one
-// merged partial per problem.
-__global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
+// Merge the segments of each problem: one CTA per (problem, head, 16 output dims), 32 segment
+// lanes x 16 dims.  Every thread issues the loads of its (up to 8 per batch) segments before
+// using any of them, so up to 256 segments cost one memory round trip, then merges them with a
+// running log-sum-exp; the 32 lanes combine through shared memory.  mode 0: normalised output
+// rows (problems with a single segment were written by the main kernel); mode 1: one merged
+// partial per problem.
+__global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
   g4a::pdl_wait_primary();
   const int prob = blockIdx.x, h = blockIdx.y;
   const int hd = p.hd;
@@ -593,14 +612,12 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams 
   }
   const int2 r = p.seg_range[prob];
   if (mode == 0 && r.x == r.y) return;  // single segment: the main kernel wrote the row
-  // Loads of a batch of 8 segments per thread are issued before any of them is used (clamped
-  // addresses stay inside the range), so a batch costs one memory round trip.
   float M = -INFINITY, L = 0.f, acc = 0.f;
-  for (int base = r.x + sg; base <= r.y; base += 16 * 8) {
+  for (int base = r.x + sg; base <= r.y; base += 32 * 8) {
     float mv[8], lv[8], ov[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-      const int s = base + 16 * i;
+      const int s = base + 32 * i;
       const float* row = p.part + (size_t)(s <= r.y ? s : r.x) * prow;
       mv[i] = row[h];
       lv[i] = row[kGroup + h];
@@ -618,7 +635,7 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams 
       M = Mn;
     }
   }
-  __shared__ float sM[16][16], sL[16][16], sA[16][16];
+  __shared__ float sM[32][16], sL[32][16], sA[32][16];
   sM[sg][dl] = M;
   sL[sg][dl] = L;
   sA[sg][dl] = acc;
@@ -626,10 +643,10 @@ __global__ void __launch_bounds__(256) merge_segments_kernel(const DecodeParams 
   if (sg == 0) {
     float Mt = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 16; i++) Mt = fmaxf(Mt, sM[i][dl]);
+    for (int i = 0; i < 32; i++) Mt = fmaxf(Mt, sM[i][dl]);
     float Lt = 0.f, At = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
+    for (int i = 0; i < 32; i++) {
       const float mi = sM[i][dl];
       if (mi == -INFINITY) continue;
       const float w = exp2f(mi - Mt);
@@ -851,7 +868,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   const bool need_merge = (mode == 1) || grid > 1 || stages_upper == 0 || P > 1;
   if (need_merge) {
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_MERGE);
-    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 16), dim3(256), 0, ctx->stream,
+    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 16), dim3(512), 0, ctx->stream,
                                stages_upper > 0, p, mode, part_out);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch merge_segments_kernel");
   }

@@ -93,7 +93,11 @@ class Context:
         return self._h
 
     def set_stream(self, cuda_stream: int | None) -> None:
-        call("g4a_set_stream", self._h, c_void_p(cuda_stream))
+        """Run on a cudaStream_t handle (0 or None = the legacy default stream)."""
+        call("g4a_set_stream", self._h, c_void_p(cuda_stream or None))
+
+    def use_own_stream(self) -> None:
+        call("g4a_use_own_stream", self._h)
 
     def sync(self, timeout_ms: int = 60000) -> None:
         call("g4a_sync", self._h, int(timeout_ms))

@@ -43,6 +43,7 @@ SIGNATURES: dict[str, list] = {
     "g4a_create": [c_int, POINTER(c_void_p)],
     "g4a_destroy": [_p],
     "g4a_set_stream": [_p, _p],
+    "g4a_use_own_stream": [_p],
     "g4a_sync": [_p, _u32],
     "g4a_alloc": [_p, c_size_t, POINTER(c_void_p)],
     "g4a_free": [_p, _p],

@@ -68,8 +68,10 @@ const char* g4a_last_error(void);
 /* Library version string, e.g. "g4attn 0.1.0 sm_100a". */
 const char* g4a_version(void);
 
-/* Run subsequent calls on a caller-owned cudaStream_t (NULL restores the context's own). */
+/* Run subsequent calls on a caller-owned cudaStream_t (0 = the legacy default stream), or
+ * back on the context's own non-blocking stream. */
 g4a_status g4a_set_stream(g4a_ctx* ctx, void* cuda_stream);
+g4a_status g4a_use_own_stream(g4a_ctx* ctx);
 void* g4a_get_stream(g4a_ctx* ctx);
 
 /* Wait for all work on the context's stream, at most timeout_ms milliseconds (0 = poll once).
