@@ -68,6 +68,8 @@ struct DecodeParams {
   int2* seg_range;    // [P] first/last segment id of each problem
   float* out;         // [P * 8, hd]; null in partial mode
   int* err;
+  int kps;            // keys per stage of the launched main kernel
+  int main_grid;      // grid of the launched main kernel
 };
 
 __device__ __forceinline__ uint32_t seq_len_of(const DecodeParams& p, int seq) {
@@ -116,17 +118,17 @@ __device__ __forceinline__ const __half* row_ptr(const DecodeParams& p, const __
 // hit 8 different bank groups without padding.
 template <int HD>
 struct Cfg {
-  static constexpr int NDQ = (HD == 128) ? 2 : 4;      // output-dim slices
-  static constexpr int DPW = HD / NDQ;                 // output dims per warp
+  static constexpr int NDQ = HD / 128;                 // score k-slices = output-dim slices
+  static constexpr int DPW = 128;                      // output dims per warp
   static constexpr int NT = DPW / 8;                   // n-tiles of the p*V MMA per warp
   static constexpr int NKG = kWarps / NDQ;             // key groups of 16 keys
-  static constexpr int KPS = 16 * NKG;                 // keys per stage
+  static constexpr int KPS = 16 * NKG;                 // keys per stage (64 KB of K+V)
   static constexpr int KSTEPS = HD / 16;               // k-steps of the score MMA
   static constexpr int KPW = KSTEPS / NDQ;             // k-steps of the score MMA per warp
   static constexpr int NCB = HD / 64;                  // 64-dim column boxes per row
   static constexpr int CB_BYTES = KPS * 128;           // one column box of a stage
   static constexpr int STAGE_BYTES = 2 * NCB * CB_BYTES;  // K boxes then V boxes
-  static constexpr int STAGES = (HD == 512) ? 3 : 6;   // depth of the shared-memory ring
+  static constexpr int STAGES = 3;                     // depth of the shared-memory ring
   static constexpr int OSTRIDE = DPW + 4;              // floats per head row of a merge slot
   static constexpr int OSLOT = kGroup * OSTRIDE + 2 * kGroup;  // o[8][DPW+4] | m[8] | l[8]
   static constexpr int NSLOT = (NKG / 2) * NDQ;
@@ -134,7 +136,7 @@ struct Cfg {
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NSLOT * OSLOT * 4 +
                                  (size_t)SX_FLOATS * 4 + STAGES * sizeof(StageMeta) + 2 * STAGES * 8 + 64;
   static_assert(NKG >= 2 && NKG * NDQ == kWarps && NT % 2 == 0 && KPW % 4 == 0, "tile shape");
-  static_assert(CB_BYTES % 1024 == 0, "swizzle atoms");
+  static_assert(CB_BYTES % 1024 == 0 && STAGE_BYTES == 65536, "swizzle atoms / stage size");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -237,10 +239,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
   __syncthreads();
-
-  // Inputs (q, cache rows) may come from the preceding producer kernel.
-  g4a::pdl_wait_primary();
   g4a::pdl_launch_dependents();
+  // The work partition below only reads launch parameters and kv_lens.  kv_lens, q and the cache
+  // rows may be written by the preceding kernel: with a programmatic (PDL) launch, wait for it
+  // before reading any of them.
+  g4a::pdl_wait_primary();
 
   // ---- stage range [s0, s1) of this CTA over the flattened stage list (every warp computes it)
   long long S = 0;
@@ -445,17 +448,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       float4 mine = make_float4(sa0[0] + sa0[2] + sb0[0] + sb0[2], sa0[1] + sa0[3] + sb0[1] + sb0[3],
                                 sa1[0] + sa1[2] + sb1[0] + sb1[2], sa1[1] + sa1[3] + sb1[1] + sb1[3]);
       // ---- sum the NDQ partials of this key group (fixed order: identical in every warp)
-      float4* sxb = reinterpret_cast<float4*>(sx) + (size_t)(it & 1) * kWarps * 32;
-      sxb[warp * 32 + lane] = mine;
-      g4a::named_bar_sync(2 + kg, NDQ * 32);
-      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      float t[4] = {mine.x, mine.y, mine.z, mine.w};
+      if (NDQ > 1) {
+        float4* sxb = reinterpret_cast<float4*>(sx) + (size_t)(it & 1) * kWarps * 32;
+        sxb[warp * 32 + lane] = mine;
+        g4a::named_bar_sync(2 + kg, NDQ * 32);
+        t[0] = t[1] = t[2] = t[3] = 0.f;
 #pragma unroll
-      for (int d2 = 0; d2 < NDQ; d2++) {
-        const float4 x = sxb[(kg * NDQ + d2) * 32 + lane];
-        t[0] += x.x;
-        t[1] += x.y;
-        t[2] += x.z;
-        t[3] += x.w;
+        for (int d2 = 0; d2 < NDQ; d2++) {
+          const float4 x = sxb[(kg * NDQ + d2) * 32 + lane];
+          t[0] += x.x;
+          t[1] += x.y;
+          t[2] += x.z;
+          t[3] += x.w;
+        }
       }
       const int kl[4] = {kb + 2 * c, kb + 2 * c + 1, kb + 8 + 2 * c, kb + 9 + 2 * c};
       bool ok[4];
@@ -610,7 +616,13 @@ __global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams 
     }
     return;
   }
-  const int2 r = p.seg_range[prob];
+  int2 r;
+  if (p.B * p.nkh == 1) {  // one problem: its segments are the active CTAs 0 .. G-1
+    const uint32_t S = (hi + p.kps - 1) / p.kps - lo / p.kps;
+    r = make_int2(0, (int)min((uint32_t)p.main_grid, S) - 1);
+  } else {
+    r = p.seg_range[prob];
+  }
   if (mode == 0 && r.x == r.y) return;  // single segment: the main kernel wrote the row
   float M = -INFINITY, L = 0.f, acc = 0.f;
   for (int base = r.x + sg; base <= r.y; base += 32 * 8) {
@@ -852,6 +864,8 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   p.part = reinterpret_cast<float*>(ctx->workspace);
   p.seg_range = reinterpret_cast<int2*>(reinterpret_cast<char*>(ctx->workspace) + part_bytes);
   p.err = ctx->dev_err_dev;
+  p.kps = C::KPS;
+  p.main_grid = grid;
   if (stages_upper > 0) {
     // rows held by a contiguous buffer: positions [row_base, min(kv_end, kv_len))
     const uint64_t end = std::min<uint64_t>(p.kv_end, p.kv_len_scalar);
@@ -928,7 +942,7 @@ g4a_status decode_contiguous(g4a_ctx* ctx, const float* q, const uint16_t* k, co
   p.err = ctx->dev_err_dev;
   const uint32_t ws = (window != 0u && kv_len > window) ? kv_len - window : 0u;
   const long long keys = (long long)(kv_len - ws);
-  if (fast_path_ok(nqh, nkh, hd)) return dispatch_fast(ctx, p, keys * nkh + (long long)(nkh - 1) * kps_of(hd), 0, nullptr, pdl);
+  if (fast_path_ok(nqh, nkh, hd)) return dispatch_fast(ctx, p, keys * nkh + (long long)(nkh - 1) * kps_of(hd), 0, nullptr, true);
   g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<nqh, 256, 0, ctx->stream>>>(p, 0, nullptr);
   return g4a_check_launch("decode_generic_kernel");
@@ -987,7 +1001,7 @@ g4a_status g4a_decode_attn_paged(g4a_ctx* ctx, const float* q, const uint16_t* k
     }
     // Stages are counted per problem: pad one stage per problem for ragged tails.
     keys = keys * num_kv_heads + (long long)batch * num_kv_heads * kps_of(head_dim);
-    return dispatch_fast(ctx, p, keys, 0, nullptr, false);
+    return dispatch_fast(ctx, p, keys, 0, nullptr, true);
   }
   g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<batch * num_q_heads, 256, 0, ctx->stream>>>(p, 0, nullptr);
@@ -1012,7 +1026,7 @@ g4a_status g4a_decode_attn_partial(g4a_ctx* ctx, const float* q, const uint16_t*
   const uint32_t hi = kv_len_total < kv_end ? kv_len_total : kv_end;
   const long long keys = hi > lo ? (long long)(hi - lo) : 0;
   if (num_kv_heads == 1 && fast_path_ok(num_q_heads, num_kv_heads, head_dim))
-    return dispatch_fast(ctx, p, keys, 1, part, false);
+    return dispatch_fast(ctx, p, keys, 1, part, true);
   g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<num_q_heads, 256, 0, ctx->stream>>>(p, 1, part);
   return g4a_check_launch("decode_generic_kernel(partial)");
