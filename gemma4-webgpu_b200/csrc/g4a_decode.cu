@@ -178,20 +178,21 @@ __device__ __forceinline__ uint32_t pack_f16(float a, float b) {
   return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
 }
 // Tiled TMA loads (no multicast) completing on an mbarrier, with an L2 cache hint.
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                            uint64_t* bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(g4a::smem_u32(bar)), "l"(pol)
-      : "memory");
-}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                             uint64_t* bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
       "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(g4a::smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            int c4, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(g4a::smem_u32(bar)),
+      "l"(pol)
       : "memory");
 }
 
@@ -344,24 +345,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)__popc(need_mask) * (uint32_t)(BR * 128 * NCB * 2));
     }
     __syncwarp();
-    // One op per (sub-box, column box, tensor), spread over the lanes.
-    const int nops = nsub * NCB * 2;
-    for (int op = lane; op < nops; op += 32) {
-      const int s = op / (NCB * 2);
-      if (!((need_mask >> s) & 1u)) continue;
-      const int rem = op % (NCB * 2);
-      const int cb = rem >> 1;
-      const bool is_v = rem & 1;
-      const uint32_t dst = (is_v ? sV : sK) + cb * CBB + s * BR * 128;
-      const CUtensorMap* map = is_v ? &tmv : &tmk;
-      if (p.page_table) {
-        // page id of sub-box s (lane s validated it above; the table line is in L1)
-        const uint32_t pos = key0 + (uint32_t)(s * BR);
-        const int page = p.page_table[(size_t)seq * p.max_pages + pos / (uint32_t)p.page_size];
-        tma_load_4d(dst, map, cb * 64, kvh, (int)(pos % (uint32_t)p.page_size), page, &full[slot], pol);
-      } else {
-        const int row = (int)key0 - (int)p.row_base;
-        tma_load_3d(dst, map, cb * 64, kvh, row, &full[slot], pol);
+    // One op per (sub-box, tensor): each op fills the sub-box rows of all HD/64 column boxes.
+    if (lane < 2 * nsub) {
+      const int s = lane >> 1;
+      const bool is_v = lane & 1;
+      if ((need_mask >> s) & 1u) {
+        const uint32_t dst = (is_v ? sV : sK) + s * NCB * BR * 128;  // sub-box s: [chunk][BR][128 B]
+        const CUtensorMap* map = is_v ? &tmv : &tmk;
+        if (p.page_table) {
+          // page id of sub-box s (lane s validated it above; the table line is in L1)
+          const uint32_t pos = key0 + (uint32_t)(s * BR);
+          const int page = p.page_table[(size_t)seq * p.max_pages + pos / (uint32_t)p.page_size];
+          tma_load_5d(dst, map, 0, kvh, (int)(pos % (uint32_t)p.page_size), page, 0, &full[slot], pol);
+        } else {
+          tma_load_4d(dst, map, 0, kvh, (int)key0 - (int)p.row_base, 0, &full[slot], pol);
+        }
       }
     }
     if (++j == nprob) {  // advance the cursor to the next problem with stages
@@ -389,14 +387,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   float m_run = -INFINITY;    // running max of head g (base 2)
   float l_part = 0.f;         // this thread's share of the running sum of head g
   bool seg_whole_start = false;
-  // ldmatrix lanes: matrix mi = lane/8, row r8 = lane%8.  In a swizzled box, 16-byte chunk ch of
-  // row r sits at chunk ch ^ (r & 7); every row below is a multiple of 8 plus r8.
+  // ldmatrix lanes: matrix mi = lane/8, row r8 = lane%8.  A stage tensor is a sequence of
+  // sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller), each holding its
+  // rows of every 64-dim column chunk as [chunk][BR rows][128 B] with the 128-byte swizzle
+  // (16-byte chunk ch of row r stored at ch ^ (r & 7)); every row below is 8-aligned plus r8.
   const int mi = lane >> 3, r8 = lane & 7;
+  const int BRc = p.page_table ? min(p.page_size, KPS) : KPS;
+  const uint32_t cstride = (uint32_t)BRc * 128;  // bytes between column chunks of a sub-box
+  auto row_off = [&](int row) -> uint32_t {
+    return (uint32_t)(row / BRc) * (NCB * cstride) + (uint32_t)(row % BRc) * 128;
+  };
   // K (non-trans): matrices (keys 0-7 | 8-15) x (dims +0 | +8) of a 16-dim k-step.
-  const uint32_t k_row = (uint32_t)(kg * 16 + r8 + 8 * (mi >> 1)) * 128;
+  const uint32_t k_row = row_off(kg * 16 + r8 + 8 * (mi >> 1));
   const int k_chunk = (mi & 1) ^ r8;  // chunk of k-step 0; k-step ks adds 2*(ks&3) by XOR
   // V (trans): matrices (keys 0-7 | 8-15) x (dims +0 | +8) of a 16-dim pair of n-tiles.
-  const uint32_t v_row = (uint32_t)(kg * 16 + r8 + 8 * (mi & 1)) * 128;
+  const uint32_t v_row = row_off(kg * 16 + r8 + 8 * (mi & 1));
   const int v_chunk = (mi >> 1) ^ r8;
 
   for (int it = 0; it < my_stages; it++) {
@@ -436,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < KPW; j += 2) {
         uint32_t b00, b01, b10, b11, c00, c01, c10, c11;
-        const uint32_t box = sK + (dq * (KPW / 4) + (j >> 2)) * CBB + k_row;
+        const uint32_t box = sK + (dq * (KPW / 4) + (j >> 2)) * cstride + k_row;
         ldsm_x4(box + ((k_chunk ^ (2 * (j & 3))) << 4), b00, b01, b10, b11);
         ldsm_x4(box + ((k_chunk ^ (2 * ((j + 1) & 3))) << 4), c00, c01, c10, c11);
         mma_16816(sa0, qa[j][0], qa[j][1], qa[j][2], qa[j][3], b00, b01);
@@ -506,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int np = 0; np < NT / 2; np++) {
         const int dim = dq * DPW + np * 16;  // first dim of the pair of n-tiles
-        const uint32_t box = sV + (dim >> 6) * CBB + v_row;
+        const uint32_t box = sV + (dim >> 6) * cstride + v_row;
         uint32_t b00, b01, b10, b11;
         ldsm_x4_trans(box + ((v_chunk ^ ((dim & 63) >> 3)) << 4), b00, b01, b10, b11);
         mma_16816(o[2 * np], pa0, pa1, pa2, pa3, b00 & mlo, b01 & mhi);
@@ -819,33 +824,37 @@ g4a_status get_encoder(g4a_ctx* ctx, PFN_cuTensorMapEncodeTiled_v12000* out) {
   return G4A_OK;
 }
 
-// Tensor maps of the K and V caches: 64-dim x 1-head x KPS-row boxes (or page-sized boxes) with
-// the 128-byte swizzle, zero fill outside the tensor.  Contiguous: [rows, nkh, hd] with rows =
-// the positions held by the buffer.  Paged: [num_pages, page_size, nkh, hd].
+// Tensor maps of the K and V caches.  The 64-element column chunk of a row is the innermost
+// dimension and the chunk index the outermost one (stride 128 B), so one box of {64, rows, HD/64
+// chunks} lands in shared memory as HD/64 column boxes of [rows x 128 B] -- the layout the
+// consumers read -- with the 128-byte swizzle, and a stage costs one TMA op per tensor.
+// Contiguous: {64, nkh, rows, chunks}; paged: {64, nkh, page_size, num_pages, chunks}.
+// Elements outside the tensor are zero-filled.
 g4a_status encode_kv_maps(g4a_ctx* ctx, const DecodeParams& p, int kps, uint64_t rows, CUtensorMap* mk,
                           CUtensorMap* mv) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   if (g4a_status s = get_encoder(ctx, &enc)) return s;
-  const cuuint64_t hd = (cuuint64_t)p.hd, nkh = (cuuint64_t)p.nkh;
-  cuuint64_t dims[4], strides[3];
-  cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
+  const cuuint64_t hd = (cuuint64_t)p.hd, nkh = (cuuint64_t)p.nkh, ncb = hd / 64;
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], estr[5] = {1, 1, 1, 1, 1};
   cuuint32_t rank;
   if (p.page_table) {
-    rank = 4;
-    dims[0] = hd; dims[1] = nkh; dims[2] = (cuuint64_t)p.page_size; dims[3] = (cuuint64_t)p.num_pages;
-    strides[0] = hd * 2; strides[1] = nkh * hd * 2; strides[2] = (cuuint64_t)p.page_size * nkh * hd * 2;
-    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)std::min(p.page_size, kps); box[3] = 1;
+    rank = 5;
+    dims[0] = 64; dims[1] = nkh; dims[2] = (cuuint64_t)p.page_size; dims[3] = (cuuint64_t)p.num_pages; dims[4] = ncb;
+    strides[0] = hd * 2; strides[1] = nkh * hd * 2; strides[2] = (cuuint64_t)p.page_size * nkh * hd * 2; strides[3] = 128;
+    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)std::min(p.page_size, kps); box[3] = 1; box[4] = (cuuint32_t)ncb;
   } else {
-    rank = 3;
-    dims[0] = hd; dims[1] = nkh; dims[2] = rows;
-    strides[0] = hd * 2; strides[1] = nkh * hd * 2;
-    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)kps;
+    rank = 4;
+    dims[0] = 64; dims[1] = nkh; dims[2] = rows; dims[3] = ncb;
+    strides[0] = hd * 2; strides[1] = nkh * hd * 2; strides[2] = 128;
+    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)kps; box[3] = (cuuint32_t)ncb;
   }
   for (int t = 0; t < 2; t++) {
     CUresult r = enc(t ? mv : mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<__half*>(t ? p.v : p.k), dims,
                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled failed (%d) for the %s cache", (int)r, t ? "V" : "K");
+    if (r != CUDA_SUCCESS)
+      return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled failed (%d) for the %s cache", (int)r, t ? "V" : "K");
   }
   return G4A_OK;
 }
