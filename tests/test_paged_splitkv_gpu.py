@@ -56,6 +56,28 @@ def test_paged_batch_matches_oracle(ctx, oracle, page_size, W):
             assert_attention_close(ours[b], ref, what=f"seq {b} L={L} ps={page_size} W={W}")
 
 
+@pytest.mark.parametrize("W", [0, 512])
+def test_paged_long_sequence_among_short(ctx, oracle, W):
+    """One sequence long enough to be split over many CTAs (two-level merge) next to short and
+    empty ones; run twice in a row so that the merge counters are seen to reset."""
+    lengths = np.array([1, 70000, 0, 2500, 700, 64], dtype=np.int32)
+    q, kp, vp, table, caches = _paged_setup(ctx, oracle, lengths, 64, 1e4 if W else 1e6, seed=21)
+    for rep in range(2):
+        out = torch.full((len(lengths), 8, 256), float("nan"), device="cuda")
+        ctx.decode_attn_paged(dev(q), kp, vp, dev(table), dev(lengths), out, num_q_heads=8, num_kv_heads=1,
+                              head_dim=256, page_size=64, sliding_window=W, host_kv_lens=lengths)
+        ctx.sync()
+        ours = host(out)
+        for b, L in enumerate(lengths):
+            if L == 0:
+                assert not ours[b].any()
+                continue
+            k, v = caches[b]
+            ref = oracle.decode_attn_f64(q[b], k, v, num_q_heads=8, num_kv_heads=1, head_dim=256, kv_len=int(L),
+                                         sliding_window=W)
+            assert_attention_close(ours[b], ref, what=f"rep {rep} seq {b} L={L} W={W}")
+
+
 def test_config3_shape_reduced(ctx, oracle):
     """64 sequences, 64-token pages in a seeded random order, one sliding and one global layer."""
     lengths = synth.batched_lengths(2, 64, 1024, 4096)
