@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ncu-case", type=int, default=0, metavar="L",
+                    help="small profiling workload: two L-token caches, six decode_attn calls, no timing")
     return ap.parse_args()
 
 
@@ -485,8 +487,27 @@ def run_sweep(ctx, torch, args):
     return out
 
 
+def run_ncu_case(L: int) -> int:
+    """A few launches on a small device footprint (two caches of L tokens), for ncu captures."""
+    import torch
+
+    import g4attn
+
+    with g4attn.Context(0) as ctx:
+        kcs, vcs, qs = build_layers(ctx, torch, L, 2, seed=1)
+        out = torch.zeros((NQH, HD), device="cuda")
+        for i in range(6):
+            ctx.decode_attn(qs[i % 2], kcs[i % 2], vcs[i % 2], out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                            seq_len=L)
+        ctx.sync()
+        print(json.dumps({"ncu_case": L, "out_abs_sum": float(out.abs().sum())}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.ncu_case:
+        return run_ncu_case(args.ncu_case)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
