@@ -27,6 +27,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include <cudaTypedefs.h>
 
@@ -859,8 +860,17 @@ g4a_status encode_kv_maps(g4a_ctx* ctx, const DecodeParams& p, int kps, uint64_t
   return G4A_OK;
 }
 
+// A scratch area of fixed size supplied by the caller instead of the context's growable
+// workspace (used by g4a_decode_attn_noalloc).
+struct FixedScratch {
+  void* ptr;
+  size_t bytes;
+  const char* who;  // entry-point name for error messages
+};
+
 template <int HD>
-g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, int mode, float* part_out, bool pdl) {
+g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, int mode, float* part_out, bool pdl,
+                       const FixedScratch* fixed) {
   using C = Cfg<HD>;
   if (g4a_status s = configure_kernel<HD>(ctx)) return s;
   const int P = p.B * p.nkh;
@@ -869,9 +879,21 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   const size_t prow = (size_t)kGroup * (HD + 2) * sizeof(float);
   const size_t segs = (size_t)grid + (size_t)P + 1;
   const size_t part_bytes = (segs * prow + 255) & ~size_t(255);
-  if (g4a_status s = g4a_ensure_workspace(ctx, part_bytes + (size_t)P * sizeof(int2) + 256)) return s;
-  p.part = reinterpret_cast<float*>(ctx->workspace);
-  p.seg_range = reinterpret_cast<int2*>(reinterpret_cast<char*>(ctx->workspace) + part_bytes);
+  const size_t need = part_bytes + (size_t)P * sizeof(int2) + 256;
+  char* ws;
+  if (fixed) {  // caller-provided scratch of fixed size: never grown
+    if (need > fixed->bytes)
+      return g4a_fail(G4A_EINVAL,
+                      "%s: this call needs %zu bytes of split-KV scratch (num_kv_heads %d, head_dim %d, %d CTAs) "
+                      "but the fixed scratch area holds %zu bytes",
+                      fixed->who, need, p.nkh, HD, grid, fixed->bytes);
+    ws = static_cast<char*>(fixed->ptr);
+  } else {
+    if (g4a_status s = g4a_ensure_workspace(ctx, need)) return s;
+    ws = static_cast<char*>(ctx->workspace);
+  }
+  p.part = reinterpret_cast<float*>(ws);
+  p.seg_range = reinterpret_cast<int2*>(ws + part_bytes);
   p.err = ctx->dev_err_dev;
   p.kps = C::KPS;
   p.main_grid = grid;
@@ -899,14 +921,15 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
 }
 
 // keys_upper: an upper bound on the total number of visible (problem, key) pairs.
-g4a_status dispatch_fast(g4a_ctx* ctx, DecodeParams& p, long long keys_upper, int mode, float* part_out, bool pdl) {
+g4a_status dispatch_fast(g4a_ctx* ctx, DecodeParams& p, long long keys_upper, int mode, float* part_out, bool pdl,
+                         const FixedScratch* fixed = nullptr) {
   switch (p.hd) {
     case 128:
-      return launch_fast<128>(ctx, p, (keys_upper + Cfg<128>::KPS - 1) / Cfg<128>::KPS, mode, part_out, pdl);
+      return launch_fast<128>(ctx, p, (keys_upper + Cfg<128>::KPS - 1) / Cfg<128>::KPS, mode, part_out, pdl, fixed);
     case 256:
-      return launch_fast<256>(ctx, p, (keys_upper + Cfg<256>::KPS - 1) / Cfg<256>::KPS, mode, part_out, pdl);
+      return launch_fast<256>(ctx, p, (keys_upper + Cfg<256>::KPS - 1) / Cfg<256>::KPS, mode, part_out, pdl, fixed);
     case 512:
-      return launch_fast<512>(ctx, p, (keys_upper + Cfg<512>::KPS - 1) / Cfg<512>::KPS, mode, part_out, pdl);
+      return launch_fast<512>(ctx, p, (keys_upper + Cfg<512>::KPS - 1) / Cfg<512>::KPS, mode, part_out, pdl, fixed);
     default:
       return g4a_fail(G4A_EINVAL, "decode: unsupported head_dim %d", p.hd);
   }
@@ -944,17 +967,52 @@ DecodeParams base_params(const float* q, const uint16_t* k, const uint16_t* v, u
 
 g4a_status decode_contiguous(g4a_ctx* ctx, const float* q, const uint16_t* k, const uint16_t* v, float* out,
                              uint32_t nqh, uint32_t nkh, uint32_t hd, uint32_t kv_len, float scale, uint32_t window,
-                             bool pdl) {
+                             bool pdl, const FixedScratch* fixed = nullptr) {
   DecodeParams p = base_params(q, k, v, nqh, nkh, hd, scale, window, out);
   p.B = 1;
   p.kv_len_scalar = kv_len;
   p.err = ctx->dev_err_dev;
   const uint32_t ws = (window != 0u && kv_len > window) ? kv_len - window : 0u;
   const long long keys = (long long)(kv_len - ws);
-  if (fast_path_ok(nqh, nkh, hd)) return dispatch_fast(ctx, p, keys * nkh + (long long)(nkh - 1) * kps_of(hd), 0, nullptr, true);
+  if (fast_path_ok(nqh, nkh, hd))
+    return dispatch_fast(ctx, p, keys * nkh + (long long)(nkh - 1) * kps_of(hd), 0, nullptr, true, fixed);
   g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
   decode_generic_kernel<<<nqh, 256, 0, ctx->stream>>>(p, 0, nullptr);
   return g4a_check_launch("decode_generic_kernel");
+}
+
+}  // namespace
+
+// Fixed split-KV scratch of g4a_decode_attn_noalloc: enough for every single-sequence decode
+// with num_kv_heads <= 64 at head_dim <= 512 on a 148-SM B200 ((148 + 64 + 1) rows of
+// 8 * 514 floats, plus 64 segment ranges).  It occupies this much device memory on every device
+// the library's module is loaded on.
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g4a_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_noalloc_address[kMaxDevices];
+
+// Device address of g4a_noalloc_scratch on `device`, looked up once per device with that device
+// current (the caller's current device is restored afterwards).
+g4a_status noalloc_scratch_address(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices) return g4a_fail(G4A_EINVAL, "noalloc scratch: device %d out of range", device);
+  void* ptr = g_noalloc_address[device].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    int prev = -1;
+    G4A_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) G4A_CUDA_TRY(cudaSetDevice(device));
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g4a_noalloc_scratch);
+    if (prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaGetSymbolAddress(g4a_noalloc_scratch)");
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 255u) != 0)
+      return g4a_fail(G4A_ECUDA, "noalloc scratch: unexpected symbol address %p", ptr);
+    g_noalloc_address[device].store(ptr, std::memory_order_release);
+  }
+  *out = ptr;
+  return G4A_OK;
 }
 
 }  // namespace
@@ -1050,6 +1108,28 @@ g4a_status g4a_lse_merge(g4a_ctx* ctx, const float* parts, uint32_t n_parts, uin
   g4a_prof_scope ps(ctx, G4A_PROF_LSE_MERGE);
   lse_merge_kernel<<<num_q_heads, 256, 0, ctx->stream>>>(parts, (int)n_parts, (int)num_q_heads, (int)head_dim, out);
   return g4a_check_launch("lse_merge_kernel");
+}
+
+// Allocation-free variant of g4a_decode_attn (no counterpart in the reference).  The split-KV
+// partial rows and segment ranges live in g4a_noalloc_scratch below instead of the context's
+// workspace, which g4a_decode_attn grows with cudaMalloc on first use and for larger shapes.
+// Nothing in the scratch needs to start at zero: the main kernel writes every partial row and
+// segment range before the merge kernel reads it.  The first call on each device looks up the
+// scratch address (cudaGetSymbolAddress, with that device current); make that first call
+// before capturing a stream.  Calls that overlap in time on one device share the scratch and
+// race.
+g4a_status g4a_decode_attn_noalloc(g4a_ctx* ctx, const float* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                   float* out, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                                   uint32_t kv_len, float scale, uint32_t sliding_window) {
+  G4A_CHECK_CTX(ctx);
+  if (g4a_status s = check_common(__func__, q, k_cache, v_cache, out, num_q_heads, num_kv_heads, head_dim)) return s;
+  if (ctx->prof_enabled)
+    return g4a_fail(G4A_EINVAL, "%s: the per-launch profiler creates CUDA events; disable it for this call", __func__);
+  void* scratch = nullptr;
+  if (g4a_status s = noalloc_scratch_address(ctx->device, &scratch)) return s;
+  const FixedScratch fixed = {scratch, kNoAllocScratchBytes, __func__};
+  return decode_contiguous(ctx, q, k_cache, v_cache, out, num_q_heads, num_kv_heads, head_dim, kv_len, scale,
+                           sliding_window, false, &fixed);
 }
 
 }  // extern "C"

@@ -165,6 +165,19 @@ class Context:
         call("g4a_decode_attn", self._h, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), num_q_heads,
              num_kv_heads, head_dim, int(seq_len), float(scale), int(sliding_window))
 
+    def decode_attn_noalloc(self, q, k_cache, v_cache, out, *, num_q_heads, num_kv_heads, head_dim, seq_len,
+                            scale=1.0, sliding_window=0) -> None:
+        """decode_attn with its split-KV scratch in a fixed static device area: the call
+        allocates no memory (no reference counterpart)."""
+        import torch
+
+        _check(q, "q", torch.float32, num_q_heads * head_dim, self.device)
+        _check(k_cache, "k_cache", torch.float16, seq_len * num_kv_heads * head_dim, self.device)
+        _check(v_cache, "v_cache", torch.float16, seq_len * num_kv_heads * head_dim, self.device)
+        _check(out, "out", torch.float32, num_q_heads * head_dim, self.device)
+        call("g4a_decode_attn_noalloc", self._h, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), num_q_heads,
+             num_kv_heads, head_dim, int(seq_len), float(scale), int(sliding_window))
+
     def decode_attn_paged(self, q, k_pages, v_pages, page_table, kv_lens, out, *, num_q_heads, num_kv_heads,
                           head_dim, page_size, scale=1.0, sliding_window=0, host_kv_lens=None) -> None:
         """Batched decode over a paged f16 cache (new capability; no reference counterpart)."""

@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
     "g4a_rms_norm_no_weight": [_p, _p, _u32, _u32, _f],
     "g4a_kv_store": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],
     "g4a_decode_attn": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],
+    "g4a_decode_attn_noalloc": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _f, _u32],
     "g4a_decode_attn_paged": [_p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _f, _u32, _p],
     "g4a_decode_attn_partial": [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _u32, _p],
     "g4a_lse_merge": [_p, _p, _u32, _u32, _u32, _p],

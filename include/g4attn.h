@@ -147,6 +147,23 @@ g4a_status g4a_decode_attn(g4a_ctx* ctx, const float* q, const uint16_t* k_cache
                            uint32_t num_kv_heads, uint32_t head_dim, uint32_t kv_len, float scale,
                            uint32_t sliding_window);
 
+/* g4a_decode_attn without any memory allocation (no counterpart in the reference).  For
+ * callers that must not allocate device memory inside the call: a serving loop that captures
+ * it into a CUDA graph, or a host whose device-memory budget is fixed up front.  Same arguments,
+ * semantics and results as g4a_decode_attn; its split-KV scratch is a fixed 4 MiB
+ * statically allocated device area instead of the context's workspace, which g4a_decode_attn
+ * grows with cudaMalloc.  The area fits every shape with num_kv_heads <= 64 and head_dim <= 512
+ * on a 148-SM B200; a shape that needs more is rejected with G4A_EINVAL and a message giving
+ * the bytes needed, and nothing is launched.  Nothing in the area has to start at zero.  The
+ * first call on each device looks up the area's address (cudaGetSymbolAddress): make that
+ * first call before any stream capture.  Calls that overlap in time on the same device (other
+ * streams, other contexts, other host threads) share the one area and race: serialise them.
+ * Fails with G4A_EINVAL while the context's profiler is enabled (it creates events). */
+g4a_status g4a_decode_attn_noalloc(g4a_ctx* ctx, const float* q, const uint16_t* k_cache,
+                                   const uint16_t* v_cache, float* out, uint32_t num_q_heads,
+                                   uint32_t num_kv_heads, uint32_t head_dim, uint32_t kv_len,
+                                   float scale, uint32_t sliding_window);
+
 /* Batched decode over a paged f16 cache (no reference counterpart: the reference decodes
  * one sequence, src/types.ts:636-639).  q is [batch, num_q_heads, head_dim] f32; sequence b
  * has kv_lens[b] tokens whose rows live at page page_table[b*max_pages_per_seq + t/page_size],
