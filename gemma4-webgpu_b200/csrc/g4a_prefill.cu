@@ -1,14 +1,509 @@
-// Prefill attention on the tensor cores (tcgen05.mma + TMEM).  The reference has no prefill
-// attention kernel: prefillBatched (src/engine.ts:2460-2479) runs one decode forward per token,
-// so row i equals decode attention at kv_len = start_pos + i + 1.
+// Prefill attention on the tensor cores (tcgen05.mma, TMEM accumulators, TMA tile loads).
+//
+// The reference has no prefill attention kernel: prefillBatched (src/engine.ts:2460-2479) runs
+// one decode forward per prompt token, so row i of the result is decode attention
+// (shaders/attn_score.wgsl, softmax.wgsl, attn_output.wgsl) at kv_len = start_pos + i + 1 with
+// the window measured from that kv_len.  This kernel computes the same rows as one flash-
+// attention pass.
+//
+// Tile: 128 query rows = 16 consecutive tokens x the 8 q heads that share one kv head (GQA 8:1),
+// so every row of a tile reads the same K/V rows.  One CTA per tile, heaviest (latest) tiles
+// first.  Warp roles (256 threads):
+//   warp 0 lane 0   TMA producer: the Q tile once, then K and V blocks of 64 keys into a
+//                   2-stage ring (one TMA op per tensor per block, 128-byte swizzle).
+//   warp 1          allocates TMEM; lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K = HD,
+//                   f16 in / f32 accumulate) into one of two TMEM score buffers, and
+//                   O += P_j V_j (M 128, N = HD, K 64) into the TMEM output accumulator.
+//   warps 4-7       softmax, one thread per query row (TMEM lane = row): scores from TMEM,
+//                   window/causal mask, online softmax in base 2 with lazy rescaling (O is
+//                   rescaled in TMEM only when a row's max grows by more than 2^8), P rounded to
+//                   f16 and written to shared memory in the MMA operand layout; the row sum l
+//                   accumulates the rounded P so numerator and denominator use the same weights.
+//                   Epilogue: O / l from TMEM to the f32 output.
+// S_{j+1} is issued before PV_j, so the tensor core computes the next scores while the softmax
+// warps work on the current ones.  Every mbarrier wait is bounded; after a timeout the CTA
+// records an error, stops waiting and frees its TMEM.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
 #include "g4a_internal.cuh"
+
+namespace {
+
+constexpr int kRows = 128;                 // query rows per tile (TMEM lanes)
+constexpr int kHeadsPerKv = 8;             // q heads per kv head handled by this kernel
+constexpr int kTokPerTile = kRows / kHeadsPerKv;
+constexpr int kKeys = 64;                  // keys per block
+constexpr int kStagesP = 2;                // K/V ring depth
+constexpr int kThreadsP = 256;
+constexpr float kLog2eP = 1.4426950408889634f;
+constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units)
+
+template <int HD>
+struct PCfg {
+  static constexpr int NCB = HD / 64;               // 64-dim chunks (128-byte swizzle rows)
+  static constexpr int Q_CHUNK = kRows * 128;       // bytes of one chunk of the Q tile
+  static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
+  static constexpr int Q_BYTES = NCB * Q_CHUNK;
+  static constexpr int KV_BYTES = NCB * KV_CHUNK;
+  static constexpr int P_BYTES = kRows * kKeys * 2;
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + kStagesP * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr int NBARS = 14;
+  static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
+  // TMEM columns: O accumulator [0, HD), score buffers at HD and HD + 64.
+  static constexpr uint32_t COL_S = HD;
+  static constexpr uint32_t TMEM_COLS = (HD + 2 * kKeys) <= 256 ? 256u : 512u;
+  static_assert(OFF_P % 1024 == 0 && OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "1024-byte aligned operands");
+  static_assert(HD + 2 * kKeys <= (int)TMEM_COLS, "TMEM budget");
+};
+
+struct PrefillParams {
+  float* out;            // [T, nqh, HD] f32
+  int T;
+  uint32_t start_pos;
+  int nqh, nkh;
+  int ntiles;            // tiles per kv head = ceil(T / 16)
+  float scale_log2;      // scale * log2(e)
+  uint32_t window;       // 0 = causal over the whole prefix
+  int* err;
+};
+
+// --------------------------------------------------------------------------- tcgen05 helpers
+// Shared-memory matrix descriptor (sm_100 UMMA format): start address, leading and stride byte
+// offsets (all >> 4), descriptor version 1 at bits 46-47, 128-byte swizzle (2) at bits 61-63.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with f16 A and B, f32 accumulate, M = 128.
+__host__ __device__ constexpr uint32_t f16_idesc(int n, bool b_mn_major) {
+  return (1u << 4)                              // D format f32
+         | (0u << 7) | (0u << 10)               // A, B format f16
+         | (0u << 15)                           // A K-major
+         | ((b_mn_major ? 1u : 0u) << 16)       // B major-ness
+         | ((uint32_t)(n >> 3) << 17)           // N >> 3
+         | ((uint32_t)(128 >> 4) << 24);        // M >> 4
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 operation issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   g4a::smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive TMEM columns of this warp's 32 lanes: thread i gets lane (base + i).  The
+// wait is in the same asm statement, so no use of the registers can be scheduled before the
+// data has arrived.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_4d_p(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                              uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(g4a::smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+// Bounded mbarrier wait that also gives up at once when another thread of the CTA already gave
+// up (abort flag in shared memory), so a failure costs one timeout, not one per wait.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                              int code) {
+  if (g4a::mbar_try_wait(bar, parity)) return true;
+  if (*abort_flag) return false;
+  const uint64_t t0 = g4a::globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (g4a::mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (g4a::globaltimer_ns() - t0 > 2000000000ull) {
+        *abort_flag = 1;
+        if (err) atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+// --------------------------------------------------------------------------- the kernel
+template <int HD>
+__global__ void __launch_bounds__(kThreadsP, 1)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+  using C = PCfg<HD>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* barQ = bars;            // Q tile landed
+  uint64_t* fullK = bars + 1;       // [2] K block landed
+  uint64_t* fullV = bars + 3;       // [2] V block landed
+  uint64_t* empty = bars + 5;       // [2] K/V stage consumed (tcgen05.commit)
+  uint64_t* barS = bars + 7;        // [2] score buffer ready (tcgen05.commit)
+  uint64_t* barP = bars + 9;        // [2] P block written (4 softmax warps)
+  uint64_t* barPV = bars + 11;      // [2] PV_j done (tcgen05.commit)
+  uint64_t* barEnd = bars + 13;     // every MMA of the CTA done (tcgen05.commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = (int)(blockIdx.x % (unsigned)p.nkh);
+  const int t0 = (p.ntiles - 1 - (int)(blockIdx.x / (unsigned)p.nkh)) * kTokPerTile;
+  const int t_last = min(t0 + kTokPerTile, p.T) - 1;
+  const uint32_t hi_max = p.start_pos + (uint32_t)t_last + 1u;
+  const uint32_t first_hi = p.start_pos + (uint32_t)t0 + 1u;
+  const uint32_t lo_min = (p.window != 0u && first_hi > p.window) ? first_hi - p.window : 0u;
+  const int kb0 = (int)(lo_min / kKeys);
+  const int nb = (int)((hi_max - 1u) / kKeys) - kb0 + 1;
+
+  if (threadIdx.x == 0) {
+    g4a::mbar_init(barQ, 1);
+    for (int s = 0; s < 2; s++) {
+      g4a::mbar_init(&fullK[s], 1);
+      g4a::mbar_init(&fullV[s], 1);
+      g4a::mbar_init(&empty[s], 1);
+      g4a::mbar_init(&barS[s], 1);
+      g4a::mbar_init(&barP[s], 4);
+      g4a::mbar_init(&barPV[s], 1);
+    }
+    g4a::mbar_init(barEnd, 1);
+    *abort_flag = 0;
+    g4a::fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+  }
+  if (warp == 1) {  // TMEM: one CTA per SM (shared memory), so the allocation never waits
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g4a::smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  g4a::pdl_launch_dependents();
+  // q16 and the cache rows are written by the preceding prep kernel.
+  g4a::pdl_wait_primary();
+
+  const uint32_t sbase = g4a::smem_u32(smem);
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint64_t pol_q, pol_kv;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_q));
+      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_kv));
+      g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_BYTES);
+      tma_load_4d_p(sbase, &tmq, 0, kvh * kHeadsPerKv, t0, 0, barQ, pol_q);
+      for (int j = 0; j < nb; j++) {
+        const int s = j & 1;
+        if (j >= 2 && !wait_or_abort(&empty[s], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
+                                     G4A_DEVERR_WAIT_EMPTY))
+          break;
+        const int key0 = (kb0 + j) * kKeys;
+        g4a::mbar_arrive_expect_tx(&fullK[s], (uint32_t)C::KV_BYTES);
+        tma_load_4d_p(sbase + C::OFF_K + s * C::KV_BYTES, &tmk, 0, kvh, key0, 0, &fullK[s], pol_kv);
+        g4a::mbar_arrive_expect_tx(&fullV[s], (uint32_t)C::KV_BYTES);
+        tma_load_4d_p(sbase + C::OFF_V + s * C::KV_BYTES, &tmv, 0, kvh, key0, 0, &fullV[s], pol_kv);
+      }
+      // Loads still in flight land before the CTA retires (bounded).
+      for (int j = max(0, nb - 2); j < nb; j++) {
+        (void)wait_or_abort(&fullK[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+        (void)wait_or_abort(&fullV[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
+      constexpr uint32_t idesc_pv = f16_idesc(HD, true);
+      bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!wait_or_abort(&fullK[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL))
+          return false;
+        tc_fence_after();
+        const uint32_t kbase = sbase + C::OFF_K + s * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+          const uint32_t off = (uint32_t)(kk & 3) * 32u;  // 16 dims = 32 bytes along the swizzled row
+          const uint64_t a = sw128_desc(sbase + (uint32_t)(kk >> 2) * C::Q_CHUNK + off, 16, 1024);
+          const uint64_t b = sw128_desc(kbase + (uint32_t)(kk >> 2) * C::KV_CHUNK + off, 16, 1024);
+          umma_f16(tmem + C::COL_S + (uint32_t)(s * kKeys), a, b, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&barS[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < nb; j++) {
+        const int s = j & 1;
+        if (j + 1 < nb && !issue_s(j + 1)) break;
+        if (!wait_or_abort(&barP[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+        if (!wait_or_abort(&fullV[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+        tc_fence_after();
+        const uint32_t pbase = sbase + C::OFF_P + s * C::P_BYTES;
+        const uint32_t vbase = sbase + C::OFF_V + s * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; kk++) {
+          const uint64_t a = sw128_desc(pbase + (uint32_t)kk * 32u, 16, 1024);
+          // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK
+          // apart (leading offset), 8-key row groups 1024 bytes apart (stride offset).
+          const uint64_t b = sw128_desc(vbase + (uint32_t)kk * 2048u, (uint32_t)C::KV_CHUNK, 1024);
+          umma_f16(tmem, a, b, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&barPV[s]);
+        umma_commit(&empty[s]);
+      }
+      // No MMA may still be running when TMEM is freed, also after an abort (bounded wait).
+      umma_commit(barEnd);
+      (void)g4a::mbar_wait_bounded(barEnd, 0, p.err, G4A_DEVERR_WAIT_MMA);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int r = (warp - 4) * 32 + lane;                       // tile row = TMEM lane
+    const uint32_t lane_addr = (uint32_t)((warp - 4) * 32) << 16;
+    const int tok = t0 + r / kHeadsPerKv;
+    const int head = kvh * kHeadsPerKv + (r % kHeadsPerKv);
+    const uint32_t hi = p.start_pos + (uint32_t)tok + 1u;
+    const uint32_t lo = (p.window != 0u && hi > p.window) ? hi - p.window : 0u;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb; j++) {
+      const int s = j & 1;
+      // Waits are made warp-uniform: the tcgen05.ld/st below are warp-collective.
+      ok = __all_sync(0xffffffffu, wait_or_abort(&barS[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err,
+                                                 G4A_DEVERR_WAIT_MMA));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[2][32];
+      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(s * kKeys), sv[0]);
+      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(s * kKeys) + 32u, sv[1]);
+      const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys;
+      const bool whole = key0 >= lo && key0 + kKeys <= hi;
+      float x[kKeys];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kKeys; c++) {
+        float v = __uint_as_float(sv[c >> 5][c & 31]) * p.scale_log2;
+        if (!whole && !(key0 + (uint32_t)c >= lo && key0 + (uint32_t)c < hi)) v = -INFINITY;
+        x[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      // lazy rescale: only when the row max grows by more than 2^kRescaleP
+      const bool grow = mx > m + kRescaleP;
+      const float m_new = grow ? mx : m;
+      const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
+      const bool warp_rescale = __any_sync(0xffffffffu, grow && m != -INFINITY) && j > 0;
+      if (warp_rescale) {
+        // O holds PV_0 .. PV_{j-1}; wait for the last of them, then scale this warp's rows.
+        ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag,
+                                                   p.err, G4A_DEVERR_WAIT_MMA));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; c++) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_addr + (uint32_t)(c * 32), o);
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tmem + lane_addr + (uint32_t)(c * 32), o);
+        }
+        tmem_wait_st();
+      }
+      l *= alpha;
+      m = m_new;
+      // P buffer s was last read by PV_{j-2}.
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[s], (uint32_t)((j - 2) >> 1) & 1u, abort_flag, p.err,
+                                                   G4A_DEVERR_WAIT_MMA));
+        if (!ok) break;
+      }
+      unsigned char* prow = smem + C::OFF_P + s * C::P_BYTES + r * 128;
+      float lsum = 0.f;
+#pragma unroll
+      for (int u = 0; u < kKeys / 8; u++) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float a = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[u * 8 + 2 * e] - m);
+          const float b = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[u * 8 + 2 * e + 1] - m);
+          const __half2 h = __floats2half2_rn(a, b);
+          const float2 back = __half22float2(h);
+          lsum += back.x + back.y;
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        // 128-byte swizzle: 16-byte unit u of row r sits at unit u ^ (r % 8).
+        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l += lsum;
+      g4a::fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(&barP[s]);
+    }
+    // epilogue: O / l
+    if (ok)
+      ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag,
+                                                 p.err, G4A_DEVERR_WAIT_MMA));
+    tc_fence_after();
+    const bool store = ok && tok < p.T;
+    const float inv = (l > 0.f) ? 1.0f / l : 0.f;
+    float* orow = p.out + ((size_t)tok * p.nqh + head) * HD;
+#pragma unroll 1
+    for (int c = 0; c < HD / 32; c++) {
+      uint32_t o[32];
+      tmem_ld32(tmem + lane_addr + (uint32_t)(c * 32), o);
+      if (store) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(orow + c * 32 + i) =
+              make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                          __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
+  }
+}
+
+g4a_status get_encoder_p(g4a_ctx* ctx, PFN_cuTensorMapEncodeTiled_v12000* out) {
+  if (!ctx->encode_tiled) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    ctx->encode_tiled = fn;
+  }
+  *out = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ctx->encode_tiled);
+  return G4A_OK;
+}
+
+// {64, heads, rows, chunks} f16 map with the chunk index outermost (stride 128 B), 128-byte
+// swizzle, box {64, box_heads, box_rows, chunks}: one TMA op lands a tile as `chunks` column
+// boxes of [box_heads * box_rows rows x 128 B].
+g4a_status encode_rows_map(g4a_ctx* ctx, CUtensorMap* map, const void* base, uint32_t hd, uint32_t heads,
+                           uint64_t rows, uint32_t box_heads, uint32_t box_rows, const char* what) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (g4a_status s = get_encoder_p(ctx, &enc)) return s;
+  const cuuint64_t ncb = hd / 64;
+  cuuint64_t dims[4] = {64, heads, rows, ncb};
+  cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)heads * hd * 2, 128};
+  cuuint32_t box[4] = {64, box_heads, box_rows, (cuuint32_t)ncb};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled failed (%d) for %s", (int)r, what);
+  return G4A_OK;
+}
+
+template <int HD>
+g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
+                          uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, float scale, uint32_t window) {
+  using C = PCfg<HD>;
+  static bool configured[64] = {false};
+  if (ctx->device >= 64 || !configured[ctx->device]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(prefill_attn_kernel)");
+    if (ctx->device < 64) configured[ctx->device] = true;
+  }
+  CUtensorMap mq, mk, mv;
+  if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, "q16")) return s;
+  const uint64_t rows = (uint64_t)start_pos + T;
+  if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, "the K cache")) return s;
+  if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, "the V cache")) return s;
+  PrefillParams p = {};
+  p.out = out;
+  p.T = (int)T;
+  p.start_pos = start_pos;
+  p.nqh = (int)nqh;
+  p.nkh = (int)nkh;
+  p.ntiles = (int)((T + kTokPerTile - 1) / kTokPerTile);
+  p.scale_log2 = scale * kLog2eP;
+  p.window = window;
+  p.err = ctx->dev_err_dev;
+  g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
+  cudaError_t e = g4a_launch(prefill_attn_kernel<HD>, dim3((unsigned)(p.ntiles * p.nkh)), dim3(kThreadsP), C::SMEM,
+                             ctx->stream, true, mq, mk, mv, p);
+  if (e != cudaSuccess) return g4a_cuda_fail(e, "launch prefill_attn_kernel");
+  return G4A_OK;
+}
+
+}  // namespace
 
 extern "C" g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k_cache,
                                        const uint16_t* v_cache, float* out, uint32_t T, uint32_t start_pos,
                                        uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim, float scale,
                                        uint32_t sliding_window) {
   G4A_CHECK_CTX(ctx);
-  (void)q16; (void)k_cache; (void)v_cache; (void)out; (void)T; (void)start_pos; (void)num_q_heads;
-  (void)num_kv_heads; (void)head_dim; (void)scale; (void)sliding_window;
-  return g4a_fail(G4A_EUNSUPPORTED, "g4a_prefill_attn: tensor-core prefill kernel not built yet");
+  if (!q16 || !k_cache || !v_cache || !out) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: null pointer");
+  if (num_kv_heads == 0 || num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads)
+    return g4a_fail(G4A_EUNSUPPORTED, "g4a_prefill_attn: needs num_q_heads = 8 * num_kv_heads (got %u / %u)",
+                    num_q_heads, num_kv_heads);
+  if (head_dim != 128 && head_dim != 256)
+    return g4a_fail(G4A_EUNSUPPORTED, "g4a_prefill_attn: head_dim %u (supported: 128, 256)", head_dim);
+  if ((((uintptr_t)q16) | ((uintptr_t)k_cache) | ((uintptr_t)v_cache) | ((uintptr_t)out)) & 15u)
+    return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: pointers must be 16-byte aligned");
+  if ((uint64_t)start_pos + T > 0xffffffffull) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: start_pos + T overflows");
+  if (T == 0) return G4A_OK;
+  if (head_dim == 256)
+    return launch_prefill<256>(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
+                               sliding_window);
+  return launch_prefill<128>(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
+                             sliding_window);
 }
