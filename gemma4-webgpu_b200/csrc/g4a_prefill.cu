@@ -1,4 +1,5 @@
-// Prefill attention on the tensor cores (tcgen05.mma, TMEM accumulators, TMA tile loads).
+// Prefill attention on the tensor cores (tcgen05.mma, TMEM operands and accumulators, TMA tile
+// loads).
 //
 // The reference has no prefill attention kernel: prefillBatched (src/engine.ts:2460-2479) runs
 // one decode forward per prompt token, so row i of the result is decode attention
@@ -8,21 +9,27 @@
 //
 // Tile: 128 query rows = 16 consecutive tokens x the 8 q heads that share one kv head (GQA 8:1),
 // so every row of a tile reads the same K/V rows.  One CTA per tile, heaviest (latest) tiles
-// first.  Warp roles (256 threads):
-//   warp 0 lane 0   TMA producer: the Q tile once, then K and V blocks of 64 keys into a
-//                   2-stage ring (one TMA op per tensor per block, 128-byte swizzle).
+// first.  The MMAs are bound by shared-memory bandwidth (128 B/clk/SM) when both operands come
+// from shared memory, so the M-side operands live in TMEM: Q (loaded once) and P (each block),
+// and shared memory carries only the K and V blocks.  TMEM columns (HD 256): O [0, 256),
+// Q [256, 384) as f16 pairs, S [384, 448), P [448, 480) as f16 pairs, l [480, 496).
+// Warp roles (384 threads):
+//   warp 0 lane 0   TMA producer of K blocks (64 keys) into a 3-stage ring; a stage is released
+//                   as soon as S_j has been computed from it.
+//   warp 2 lane 0   TMA producer of V blocks into their own 3-stage ring (released after PV_j).
 //   warp 1          allocates TMEM; lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K = HD,
-//                   f16 in / f32 accumulate) into one of two TMEM score buffers, and
-//                   O += P_j V_j (M 128, N = HD, K 64) into the TMEM output accumulator.
-//   warps 4-7       softmax, one thread per query row (TMEM lane = row): scores from TMEM,
-//                   window/causal mask, online softmax in base 2 with lazy rescaling (O is
-//                   rescaled in TMEM only when a row's max grows by more than 2^8), P rounded to
-//                   f16 and written to shared memory in the MMA operand layout; the row sum l
-//                   accumulates the rounded P so numerator and denominator use the same weights.
-//                   Epilogue: O / l from TMEM to the f32 output.
-// S_{j+1} is issued before PV_j, so the tensor core computes the next scores while the softmax
-// warps work on the current ones.  Every mbarrier wait is bounded; after a timeout the CTA
-// records an error, stops waiting and frees its TMEM.
+//                   f16 in / f32 accumulate, A from TMEM), then O += P_{j-1} V_{j-1} (N = HD)
+//                   and l += P_{j-1} x ones (N = 16), both with A = P from TMEM.
+//   warps 4-11      Q into TMEM at the start; then softmax, two threads per query row (TMEM
+//                   lane = row; warps w and w+4 take keys 0-31 and 32-63 of a block and exchange
+//                   row maxima through shared memory): scores from TMEM (the S buffer is handed
+//                   back right after the load), window/causal mask, online softmax in base 2
+//                   with lazy rescaling (O and l are rescaled in TMEM only when a row's max grows
+//                   by more than 2^8), P rounded to f16 into TMEM.  l is accumulated by the
+//                   tensor core from the same f16 P as the output, so numerator and denominator
+//                   use identical weights.  Epilogue: O / l from TMEM to the f32 output.
+// Every mbarrier wait is bounded; after a timeout the CTA records an error, stops waiting and
+// frees its TMEM.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -35,33 +42,37 @@ constexpr int kRows = 128;                 // query rows per tile (TMEM lanes)
 constexpr int kHeadsPerKv = 8;             // q heads per kv head handled by this kernel
 constexpr int kTokPerTile = kRows / kHeadsPerKv;
 constexpr int kKeys = 64;                  // keys per block
-constexpr int kStagesP = 2;                // K/V ring depth
-constexpr int kThreadsP = 256;
+constexpr int kStagesP = 3;                // K and V ring depth
+constexpr int kThreadsP = 384;
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units)
 
 template <int HD>
 struct PCfg {
   static constexpr int NCB = HD / 64;               // 64-dim chunks (128-byte swizzle rows)
-  static constexpr int Q_CHUNK = kRows * 128;       // bytes of one chunk of the Q tile
   static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
-  static constexpr int Q_BYTES = NCB * Q_CHUNK;
   static constexpr int KV_BYTES = NCB * KV_CHUNK;
-  static constexpr int P_BYTES = kRows * kKeys * 2;
-  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + kStagesP * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr int NBARS = 14;
+  static constexpr int OFF_ONES = OFF_V + kStagesP * KV_BYTES;  // 512 B of f16 ones (l MMA operand)
+  static constexpr int OFF_RED = OFF_ONES + 512;                // [2 halves][128 rows] row maxima
+  static constexpr int OFF_BAR = OFF_RED + 2 * kRows * 4;
+  static constexpr int NBARS = 20;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
-  // TMEM columns: O accumulator [0, HD), score buffers at HD and HD + 64.
-  static constexpr uint32_t COL_S = HD;
-  static constexpr uint32_t TMEM_COLS = (HD + 2 * kKeys) <= 256 ? 256u : 512u;
-  static_assert(OFF_P % 1024 == 0 && OFF_K % 1024 == 0 && OFF_V % 1024 == 0, "1024-byte aligned operands");
-  static_assert(HD + 2 * kKeys <= (int)TMEM_COLS, "TMEM budget");
+  // TMEM columns (32-bit each; f16 operands hold two elements per column)
+  static constexpr uint32_t COL_O = 0;
+  static constexpr uint32_t COL_Q = HD;
+  static constexpr uint32_t COL_S = HD + HD / 2;
+  static constexpr uint32_t COL_P = COL_S + kKeys;
+  static constexpr uint32_t COL_L = COL_P + kKeys / 2;
+  static constexpr uint32_t TMEM_COLS = (COL_L + 16) <= 256 ? 256u : 512u;
+  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte aligned operands");
+  static_assert(COL_L + 16 <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 struct PrefillParams {
+  const uint16_t* q16;   // [T, nqh, HD] f16
   float* out;            // [T, nqh, HD] f32
   int T;
   uint32_t start_pos;
@@ -84,6 +95,16 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
+// Descriptor of a K-major operand without swizzle: 8-row x 16-byte core matrices, the next 16
+// bytes of K `lbo_bytes` away, the next 8 rows `sbo_bytes` away.
+__device__ __forceinline__ uint64_t noswz_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
 // Instruction descriptor of kind::f16 with f16 A and B, f32 accumulate, M = 128.
 __host__ __device__ constexpr uint32_t f16_idesc(int n, bool b_mn_major) {
   return (1u << 4)                              // D format f32
@@ -94,13 +115,15 @@ __host__ __device__ constexpr uint32_t f16_idesc(int n, bool b_mn_major) {
          | ((uint32_t)(128 >> 4) << 24);        // M >> 4
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D (+)= A B^T with A from TMEM (K-major: row i in lane i, two f16 per 32-bit column) and B a
+// shared-memory descriptor.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -141,6 +164,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_4d_p(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
@@ -176,21 +207,23 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // --------------------------------------------------------------------------- the kernel
 template <int HD>
 __global__ void __launch_bounds__(kThreadsP, 1)
-    prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                        const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const PrefillParams p) {
   using C = PCfg<HD>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* barQ = bars;            // Q tile landed
-  uint64_t* fullK = bars + 1;       // [2] K block landed
-  uint64_t* fullV = bars + 3;       // [2] V block landed
-  uint64_t* empty = bars + 5;       // [2] K/V stage consumed (tcgen05.commit)
-  uint64_t* barS = bars + 7;        // [2] score buffer ready (tcgen05.commit)
-  uint64_t* barP = bars + 9;        // [2] P block written (4 softmax warps)
-  uint64_t* barPV = bars + 11;      // [2] PV_j done (tcgen05.commit)
-  uint64_t* barEnd = bars + 13;     // every MMA of the CTA done (tcgen05.commit)
+  uint64_t* fullK = bars;           // [3] K block landed
+  uint64_t* fullV = bars + 3;       // [3] V block landed
+  uint64_t* emptyK = bars + 6;      // [3] K stage consumed by S_j (tcgen05.commit)
+  uint64_t* emptyV = bars + 9;      // [3] V stage consumed by PV_j (tcgen05.commit)
+  uint64_t* barQ = bars + 12;       // Q in TMEM (8 softmax warps)
+  uint64_t* barS = bars + 13;       // S_j in TMEM (tcgen05.commit), once per block
+  uint64_t* barSfree = bars + 14;   // S_j loaded by the softmax warps (8 warps), once per block
+  uint64_t* barP = bars + 15;       // P_j in TMEM, O/l rescaled (8 warps), once per block
+  uint64_t* barPV = bars + 16;      // PV_j and l_j done (tcgen05.commit), once per block
+  uint64_t* barEnd = bars + 17;     // every MMA of the CTA done (tcgen05.commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -205,22 +238,27 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int nb = (int)((hi_max - 1u) / kKeys) - kb0 + 1;
 
   if (threadIdx.x == 0) {
-    g4a::mbar_init(barQ, 1);
-    for (int s = 0; s < 2; s++) {
+    for (int s = 0; s < kStagesP; s++) {
       g4a::mbar_init(&fullK[s], 1);
       g4a::mbar_init(&fullV[s], 1);
-      g4a::mbar_init(&empty[s], 1);
-      g4a::mbar_init(&barS[s], 1);
-      g4a::mbar_init(&barP[s], 4);
-      g4a::mbar_init(&barPV[s], 1);
+      g4a::mbar_init(&emptyK[s], 1);
+      g4a::mbar_init(&emptyV[s], 1);
     }
+    g4a::mbar_init(barQ, 8);
+    g4a::mbar_init(barS, 1);
+    g4a::mbar_init(barSfree, 8);
+    g4a::mbar_init(barP, 8);
+    g4a::mbar_init(barPV, 1);
     g4a::mbar_init(barEnd, 1);
     *abort_flag = 0;
     g4a::fence_mbar_init();
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
+  if (threadIdx.x < 128) {  // the all-ones operand of the l MMA (16 rows x 16 keys, no swizzle)
+    reinterpret_cast<uint32_t*>(smem + C::OFF_ONES)[threadIdx.x] = 0x3C003C00u;
+  }
+  g4a::fence_proxy_async_smem();
   if (warp == 1) {  // TMEM: one CTA per SM (shared memory), so the allocation never waits
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g4a::smem_u32(tmem_slot)),
                  "r"(C::TMEM_COLS)
@@ -236,172 +274,215 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   g4a::pdl_wait_primary();
 
   const uint32_t sbase = g4a::smem_u32(smem);
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------ TMA producers
     if (lane == 0) {
-      uint64_t pol_q, pol_kv;
-      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_q));
+      const bool kside = warp == 0;
+      uint64_t pol_kv;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_kv));
-      g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_BYTES);
-      tma_load_4d_p(sbase, &tmq, 0, kvh * kHeadsPerKv, t0, 0, barQ, pol_q);
+      uint64_t* empty = kside ? emptyK : emptyV;
+      uint64_t* full = kside ? fullK : fullV;
+      const CUtensorMap* map = kside ? &tmk : &tmv;
+      const uint32_t dst0 = sbase + (kside ? C::OFF_K : C::OFF_V);
       for (int j = 0; j < nb; j++) {
-        const int s = j & 1;
-        if (j >= 2 && !wait_or_abort(&empty[s], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
-                                     G4A_DEVERR_WAIT_EMPTY))
+        const int s = j % kStagesP;
+        if (j >= kStagesP && !wait_or_abort(&empty[s], (uint32_t)(j / kStagesP - 1) & 1u, abort_flag, p.err,
+                                            G4A_DEVERR_WAIT_EMPTY))
           break;
-        const int key0 = (kb0 + j) * kKeys;
-        g4a::mbar_arrive_expect_tx(&fullK[s], (uint32_t)C::KV_BYTES);
-        tma_load_4d_p(sbase + C::OFF_K + s * C::KV_BYTES, &tmk, 0, kvh, key0, 0, &fullK[s], pol_kv);
-        g4a::mbar_arrive_expect_tx(&fullV[s], (uint32_t)C::KV_BYTES);
-        tma_load_4d_p(sbase + C::OFF_V + s * C::KV_BYTES, &tmv, 0, kvh, key0, 0, &fullV[s], pol_kv);
+        g4a::mbar_arrive_expect_tx(&full[s], (uint32_t)C::KV_BYTES);
+        tma_load_4d_p(dst0 + s * C::KV_BYTES, map, 0, kvh, (kb0 + j) * kKeys, 0, &full[s], pol_kv);
       }
       // Loads still in flight land before the CTA retires (bounded).
-      for (int j = max(0, nb - 2); j < nb; j++) {
-        (void)wait_or_abort(&fullK[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
-        (void)wait_or_abort(&fullV[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
-      }
+      for (int j = max(0, nb - kStagesP); j < nb; j++)
+        (void)wait_or_abort(&full[j % kStagesP], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err,
+                            G4A_DEVERR_WAIT_FULL);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
       constexpr uint32_t idesc_pv = f16_idesc(HD, true);
-      bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!wait_or_abort(&fullK[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL))
+      constexpr uint32_t idesc_l = f16_idesc(16, false);
+      const uint64_t ones = noswz_desc(sbase + C::OFF_ONES, 128, 256);
+      // Base descriptors, built once; a K step only adds a constant to the start-address field
+      // (bits 0-13, in 16-byte units; every operand lies below 256 KB, so no carry leaves it).
+      const uint64_t dk0 = sw128_desc(sbase + C::OFF_K, 16, 1024);
+      // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK apart
+      // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
+      const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
+      bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_MMA);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % kStagesP;
+        if (!wait_or_abort(barP, (uint32_t)i & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) return false;
+        if (!wait_or_abort(&fullV[s], (uint32_t)(i / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL))
           return false;
         tc_fence_after();
-        const uint32_t kbase = sbase + C::OFF_K + s * C::KV_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++) {
-          const uint32_t off = (uint32_t)(kk & 3) * 32u;  // 16 dims = 32 bytes along the swizzled row
-          const uint64_t a = sw128_desc(sbase + (uint32_t)(kk >> 2) * C::Q_CHUNK + off, 16, 1024);
-          const uint64_t b = sw128_desc(kbase + (uint32_t)(kk >> 2) * C::KV_CHUNK + off, 16, 1024);
-          umma_f16(tmem + C::COL_S + (uint32_t)(s * kKeys), a, b, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&barS[s]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < nb; j++) {
-        const int s = j & 1;
-        if (j + 1 < nb && !issue_s(j + 1)) break;
-        if (!wait_or_abort(&barP[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
-        if (!wait_or_abort(&fullV[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
-        tc_fence_after();
-        const uint32_t pbase = sbase + C::OFF_P + s * C::P_BYTES;
-        const uint32_t vbase = sbase + C::OFF_V + s * C::KV_BYTES;
+        const uint64_t dv = dv0 + (uint64_t)((s * C::KV_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; kk++) {
-          const uint64_t a = sw128_desc(pbase + (uint32_t)kk * 32u, 16, 1024);
-          // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK
-          // apart (leading offset), 8-key row groups 1024 bytes apart (stride offset).
-          const uint64_t b = sw128_desc(vbase + (uint32_t)kk * 2048u, (uint32_t)C::KV_CHUNK, 1024);
-          umma_f16(tmem, a, b, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint32_t a = tmem + C::COL_P + (uint32_t)(kk * 8);  // 16 keys = 8 columns of f16 pairs
+          umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + C::COL_L, a, ones, idesc_l, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&barPV[s]);
-        umma_commit(&empty[s]);
+        umma_commit(barPV);
+        umma_commit(&emptyV[s]);
+        return true;
+      };
+      for (int j = 0; ok && j < nb; j++) {
+        const int s = j % kStagesP;
+        // S_j overwrites the S buffer: the softmax warps must have loaded S_{j-1}.
+        if (j > 0 && !wait_or_abort(barSfree, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+        if (!wait_or_abort(&fullK[s], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+        tc_fence_after();
+        const uint64_t dk = dk0 + (uint64_t)((s * C::KV_BYTES) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+          // K step kk: Q columns kk*8.. (16 dims as f16 pairs); K chunk kk/4, 32 bytes per step
+          const uint64_t b = dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4);
+          umma_f16_ts(tmem + C::COL_S, tmem + C::COL_Q + (uint32_t)(kk * 8), b, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(barS);
+        umma_commit(&emptyK[s]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
       }
+      if (ok) (void)issue_pv(nb - 1);
       // No MMA may still be running when TMEM is freed, also after an abort (bounded wait).
       umma_commit(barEnd);
       (void)g4a::mbar_wait_bounded(barEnd, 0, p.err, G4A_DEVERR_WAIT_MMA);
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax + epilogue
-    const int r = (warp - 4) * 32 + lane;                       // tile row = TMEM lane
-    const uint32_t lane_addr = (uint32_t)((warp - 4) * 32) << 16;
+    // ------------------------------------------------------------------ Q load, softmax, epilogue
+    const int quarter = warp & 3;                               // TMEM lane quarter of this warp
+    const int half = (warp - 4) >> 2;                           // keys [32*half, 32*half + 32) of a block
+    const int r = quarter * 32 + lane;                          // tile row = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int tok = t0 + r / kHeadsPerKv;
     const int head = kvh * kHeadsPerKv + (r % kHeadsPerKv);
     const uint32_t hi = p.start_pos + (uint32_t)tok + 1u;
     const uint32_t lo = (p.window != 0u && hi > p.window) ? hi - p.window : 0u;
-    float m = -INFINITY, l = 0.f;
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);   // [half][row]
+    // Q row (half of its dims) into TMEM as f16 pairs: column COL_Q + c holds dims 2c, 2c+1.
+    {
+      const bool valid = tok < p.T;
+      const uint4* src = reinterpret_cast<const uint4*>(p.q16 + ((size_t)tok * p.nqh + head) * HD + half * (HD / 2));
+#pragma unroll
+      for (int c = 0; c < HD / 128; c++) {  // this half's HD/2 dims: 32 columns (64 dims) per store
+        uint32_t w[32];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const uint4 v = valid ? __ldg(src + c * 8 + u) : make_uint4(0u, 0u, 0u, 0u);
+          w[4 * u] = v.x;
+          w[4 * u + 1] = v.y;
+          w[4 * u + 2] = v.z;
+          w[4 * u + 3] = v.w;
+        }
+        tmem_st32(tmem + lane_addr + C::COL_Q + (uint32_t)(half * (HD / 4) + c * 32), w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(barQ);
+    }
+    const float c2 = p.scale_log2;
+    float m = -INFINITY;
     bool ok = true;
     for (int j = 0; j < nb; j++) {
-      const int s = j & 1;
       // Waits are made warp-uniform: the tcgen05.ld/st below are warp-collective.
-      ok = __all_sync(0xffffffffu, wait_or_abort(&barS[s], (uint32_t)(j >> 1) & 1u, abort_flag, p.err,
-                                                 G4A_DEVERR_WAIT_MMA));
+      ok = __all_sync(0xffffffffu, wait_or_abort(barS, (uint32_t)j & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[2][32];
-      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(s * kKeys), sv[0]);
-      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(s * kKeys) + 32u, sv[1]);
-      const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys;
-      const bool whole = key0 >= lo && key0 + kKeys <= hi;
-      float x[kKeys];
-      float mx = -INFINITY;
+      uint32_t sv[32];
+      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(32 * half), sv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(barSfree);  // the S buffer may be overwritten now
+      const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys + 32u * half;
+      const bool whole = key0 >= lo && key0 + 32u <= hi;
+      // scaled scores x = s * scale * log2(e); masked keys -inf
+      float x[32];
 #pragma unroll
-      for (int c = 0; c < kKeys; c++) {
-        float v = __uint_as_float(sv[c >> 5][c & 31]) * p.scale_log2;
+      for (int c = 0; c < 32; c++) {
+        float v = __uint_as_float(sv[c]) * c2;
         if (!whole && !(key0 + (uint32_t)c >= lo && key0 + (uint32_t)c < hi)) v = -INFINITY;
         x[c] = v;
-        mx = fmaxf(mx, v);
       }
+      float mq[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        mq[q] = fmaxf(fmaxf(x[q], x[q + 4]), fmaxf(x[q + 8], x[q + 12]));
+        mq[q] = fmaxf(mq[q], fmaxf(fmaxf(x[q + 16], x[q + 20]), fmaxf(x[q + 24], x[q + 28])));
+      }
+      float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      // the row's other half (warp w +- 4, same lanes): exchange through shared memory
+      red[half * kRows + r] = mx;
+      g4a::named_bar_sync(1 + quarter, 64);
+      mx = fmaxf(mx, red[(half ^ 1) * kRows + r]);
+      g4a::named_bar_sync(1 + quarter, 64);  // both read before either writes the next block's max
       // lazy rescale: only when the row max grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx : m;
       const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
       const bool warp_rescale = __any_sync(0xffffffffu, grow && m != -INFINITY) && j > 0;
-      if (warp_rescale) {
-        // O holds PV_0 .. PV_{j-1}; wait for the last of them, then scale this warp's rows.
-        ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag,
-                                                   p.err, G4A_DEVERR_WAIT_MMA));
+      m = m_new;
+      // P = 2^(x - m) rounded to f16 pairs (computed before waiting for the previous PV)
+      uint32_t pw[16];
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        const float a = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[2 * e] - m);
+        const float b = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[2 * e + 1] - m);
+        const __half2 h = __floats2half2_rn(a, b);
+        pw[e] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      // P and the O/l rescale both wait for PV_{j-1} (single P buffer; O holds PV_0 .. PV_{j-1}).
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu,
+                        wait_or_abort(barPV, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA));
         if (!ok) break;
         tc_fence_after();
+      }
+      if (warp_rescale) {
+        // half 0: O columns [0, HD/2); half 1: [HD/2, HD) and the l columns
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; c++) {
+        for (int c = 0; c < HD / 64 + half; c++) {
+          const uint32_t col = (c < HD / 64) ? (uint32_t)(C::COL_O + half * (HD / 2) + c * 32) : C::COL_L;
           uint32_t o[32];
-          tmem_ld32(tmem + lane_addr + (uint32_t)(c * 32), o);
+          tmem_ld32(tmem + lane_addr + col, o);
 #pragma unroll
           for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tmem + lane_addr + (uint32_t)(c * 32), o);
-        }
-        tmem_wait_st();
-      }
-      l *= alpha;
-      m = m_new;
-      // P buffer s was last read by PV_{j-2}.
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[s], (uint32_t)((j - 2) >> 1) & 1u, abort_flag, p.err,
-                                                   G4A_DEVERR_WAIT_MMA));
-        if (!ok) break;
-      }
-      unsigned char* prow = smem + C::OFF_P + s * C::P_BYTES + r * 128;
-      float lsum = 0.f;
+          if (c < HD / 64) {
+            tmem_st32(tmem + lane_addr + col, o);
+          } else {
+            uint32_t o16[16];
 #pragma unroll
-      for (int u = 0; u < kKeys / 8; u++) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const float a = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[u * 8 + 2 * e] - m);
-          const float b = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[u * 8 + 2 * e + 1] - m);
-          const __half2 h = __floats2half2_rn(a, b);
-          const float2 back = __half22float2(h);
-          lsum += back.x + back.y;
-          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+            for (int i = 0; i < 16; i++) o16[i] = o[i];
+            tmem_st16(tmem + lane_addr + col, o16);
+          }
         }
-        // 128-byte swizzle: 16-byte unit u of row r sits at unit u ^ (r % 8).
-        *reinterpret_cast<uint4*>(prow + ((u ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l += lsum;
-      g4a::fence_proxy_async_smem();
+      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(16 * half), pw);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(&barP[s]);
+      if (lane == 0) g4a::mbar_arrive(barP);
     }
-    // epilogue: O / l
+    // epilogue: O / l, each half of the row's threads stores half of the columns
     if (ok)
-      ok = __all_sync(0xffffffffu, wait_or_abort(&barPV[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag,
-                                                 p.err, G4A_DEVERR_WAIT_MMA));
+      ok = __all_sync(0xffffffffu, wait_or_abort(barPV, (uint32_t)(nb - 1) & 1u, abort_flag, p.err,
+                                                 G4A_DEVERR_WAIT_MMA));
     tc_fence_after();
+    uint32_t lv[32];
+    tmem_ld32(tmem + lane_addr + C::COL_L, lv);
+    const float l = __uint_as_float(lv[0]);
     const bool store = ok && tok < p.T;
     const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-    float* orow = p.out + ((size_t)tok * p.nqh + head) * HD;
+    float* orow = p.out + ((size_t)tok * p.nqh + head) * HD + half * (HD / 2);
 #pragma unroll 1
-    for (int c = 0; c < HD / 32; c++) {
+    for (int c = 0; c < HD / 64; c++) {
       uint32_t o[32];
-      tmem_ld32(tmem + lane_addr + (uint32_t)(c * 32), o);
+      tmem_ld32(tmem + lane_addr + (uint32_t)(C::COL_O + half * (HD / 2) + c * 32), o);
       if (store) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
@@ -462,12 +543,12 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
     if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(prefill_attn_kernel)");
     if (ctx->device < 64) configured[ctx->device] = true;
   }
-  CUtensorMap mq, mk, mv;
-  if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, "q16")) return s;
+  CUtensorMap mk, mv;
   const uint64_t rows = (uint64_t)start_pos + T;
   if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, "the K cache")) return s;
   if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, "the V cache")) return s;
   PrefillParams p = {};
+  p.q16 = q16;
   p.out = out;
   p.T = (int)T;
   p.start_pos = start_pos;
@@ -479,7 +560,7 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   p.err = ctx->dev_err_dev;
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
   cudaError_t e = g4a_launch(prefill_attn_kernel<HD>, dim3((unsigned)(p.ntiles * p.nkh)), dim3(kThreadsP), C::SMEM,
-                             ctx->stream, true, mq, mk, mv, p);
+                             ctx->stream, true, mk, mv, p);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "launch prefill_attn_kernel");
   return G4A_OK;
 }
