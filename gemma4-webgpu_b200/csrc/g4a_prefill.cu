@@ -17,17 +17,20 @@
 //   warp 0 lane 0   TMA producer of K blocks (64 keys) into a 3-stage ring; a stage is released
 //                   as soon as S_j has been computed from it.
 //   warp 2 lane 0   TMA producer of V blocks into their own 3-stage ring (released after PV_j).
-//   warp 1          allocates TMEM; lane 0 issues the MMAs: S_j = Q K_j^T (M 128, N 64, K = HD,
-//                   f16 in / f32 accumulate, A from TMEM), then O += P_{j-1} V_{j-1} (N = HD)
-//                   and l += P_{j-1} x ones (N = 16), both with A = P from TMEM.
+//   warp 1          allocates TMEM; lane 0 issues the score MMAs S_j = Q K_j^T (M 128, N 64,
+//                   K = HD, f16 in / f32 accumulate, A from TMEM).
+//   warp 3 lane 0   issues O += P_j V_j (N = HD) and l += P_j x ones (N = 16), A = P from TMEM.
 //   warps 4-11      Q into TMEM at the start; then softmax, two threads per query row (TMEM
 //                   lane = row; warps w and w+4 take keys 0-31 and 32-63 of a block and exchange
 //                   row maxima through shared memory): scores from TMEM (the S buffer is handed
-//                   back right after the load), window/causal mask, online softmax in base 2
-//                   with lazy rescaling (O and l are rescaled in TMEM only when a row's max grows
-//                   by more than 2^8), P rounded to f16 into TMEM.  l is accumulated by the
-//                   tensor core from the same f16 P as the output, so numerator and denominator
-//                   use identical weights.  Epilogue: O / l from TMEM to the f32 output.
+//                   back right after the load), window/causal mask (boundary blocks only),
+//                   online softmax in base 2 with lazy rescaling (the running max is only raised
+//                   when a row's max grows by more than 2^8), P rounded to f16 into TMEM.  l is
+//                   accumulated by the tensor core from the same f16 P as the output, so
+//                   numerator and denominator use identical weights.  Epilogue: O / l from TMEM
+//                   to the f32 output.
+//   warps 12-15     correction: when a row's running max was raised, scale its O and l in TMEM
+//                   by 2^(m_old - m_new) after PV_{j-1} and before PV_j, off the softmax path.
 // Every mbarrier wait is bounded; after a timeout the CTA records an error, stops waiting and
 // frees its TMEM.
 #include <cudaTypedefs.h>
@@ -43,7 +46,7 @@ constexpr int kHeadsPerKv = 8;             // q heads per kv head handled by thi
 constexpr int kTokPerTile = kRows / kHeadsPerKv;
 constexpr int kKeys = 64;                  // keys per block
 constexpr int kStagesP = 3;                // K and V ring depth
-constexpr int kThreadsP = 384;
+constexpr int kThreadsP = 512;
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units)
 
@@ -56,8 +59,10 @@ struct PCfg {
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
   static constexpr int OFF_ONES = OFF_V + kStagesP * KV_BYTES;  // 512 B of f16 ones (l MMA operand)
   static constexpr int OFF_RED = OFF_ONES + 512;                // [2 halves][128 rows] row maxima
-  static constexpr int OFF_BAR = OFF_RED + 2 * kRows * 4;
-  static constexpr int NBARS = 20;
+  static constexpr int OFF_ALPHA = OFF_RED + 2 * kRows * 4;     // [2 parities][128 rows] rescale factors
+  static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
+  static constexpr int OFF_BAR = OFF_FLAG + 64;
+  static constexpr int NBARS = 23;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
   // TMEM columns (32-bit each; f16 operands hold two elements per column)
   static constexpr uint32_t COL_O = 0;
@@ -223,7 +228,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* barSfree = bars + 14;   // S_j loaded by the softmax warps (8 warps), once per block
   uint64_t* barP = bars + 15;       // P_j in TMEM, O/l rescaled (8 warps), once per block
   uint64_t* barPV = bars + 16;      // PV_j and l_j done (tcgen05.commit), once per block
-  uint64_t* barEnd = bars + 17;     // every MMA of the CTA done (tcgen05.commit)
+  uint64_t* barEnd = bars + 17;     // every score MMA done (tcgen05.commit)
+  // One barrier per block parity: the correction of block j+1 may finish before the MMA thread
+  // waits for that of block j (and the factors of j+1 may be published before the correction
+  // warps wait for those of j), so a single barrier could complete twice between two waits.
+  uint64_t* barAlpha = bars + 18;   // [2] rescale factors of block j published (4 softmax warps)
+  uint64_t* barCorr = bars + 20;    // [2] O/l rescaled for block j (4 correction warps)
+  uint64_t* barEnd2 = bars + 22;    // every PV/l MMA done (tcgen05.commit)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -250,6 +261,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     g4a::mbar_init(barP, 8);
     g4a::mbar_init(barPV, 1);
     g4a::mbar_init(barEnd, 1);
+    g4a::mbar_init(barEnd2, 1);
+    for (int s = 0; s < 2; s++) {
+      g4a::mbar_init(&barAlpha[s], 4);
+      g4a::mbar_init(&barCorr[s], 4);
+    }
     *abort_flag = 0;
     g4a::fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
@@ -297,63 +313,65 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         (void)wait_or_abort(&full[j % kStagesP], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err,
                             G4A_DEVERR_WAIT_FULL);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 3) {
+    // ------------------------------------------------------------------ MMA issuers
+    // Two issuing threads, so that the waits of one never leave the tensor pipe without work:
+    // warp 1 issues the score MMAs, warp 3 the PV and l MMAs.  Each commit tracks the MMAs of its
+    // own thread.
     if (lane == 0) {
-      constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
-      constexpr uint32_t idesc_pv = f16_idesc(HD, true);
-      constexpr uint32_t idesc_l = f16_idesc(16, false);
-      const uint64_t ones = noswz_desc(sbase + C::OFF_ONES, 128, 256);
-      // Base descriptors, built once; a K step only adds a constant to the start-address field
-      // (bits 0-13, in 16-byte units; every operand lies below 256 KB, so no carry leaves it).
-      const uint64_t dk0 = sw128_desc(sbase + C::OFF_K, 16, 1024);
-      // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK apart
-      // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
-      const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
-      bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_MMA);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % kStagesP;
-        if (!wait_or_abort(barP, (uint32_t)i & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) return false;
-        if (!wait_or_abort(&fullV[s], (uint32_t)(i / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL))
-          return false;
-        tc_fence_after();
-        const uint64_t dv = dv0 + (uint64_t)((s * C::KV_BYTES) >> 4);
+      uint64_t* my_end = (warp == 1) ? barEnd : barEnd2;
+      if (warp == 1) {
+        constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
+        // Base descriptor, built once; a K step only adds a constant to the start-address field
+        // (bits 0-13, in 16-byte units; every operand lies below 256 KB, so no carry leaves it).
+        const uint64_t dk0 = sw128_desc(sbase + C::OFF_K, 16, 1024);
+        bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_MMA);
+        for (int j = 0; ok && j < nb; j++) {
+          const int s = j % kStagesP;
+          // S_j overwrites the S buffer: the softmax warps must have loaded S_{j-1}.
+          if (j > 0 && !wait_or_abort(barSfree, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+          if (!wait_or_abort(&fullK[s], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+          tc_fence_after();
+          const uint64_t dk = dk0 + (uint64_t)((s * C::KV_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 16; kk++) {
-          const uint32_t a = tmem + C::COL_P + (uint32_t)(kk * 8);  // 16 keys = 8 columns of f16 pairs
-          umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-          umma_f16_ts(tmem + C::COL_L, a, ones, idesc_l, (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; kk++) {
+            // K step kk: Q columns kk*8.. (16 dims as f16 pairs); K chunk kk/4, 32 bytes per step
+            const uint64_t b = dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4);
+            umma_f16_ts(tmem + C::COL_S, tmem + C::COL_Q + (uint32_t)(kk * 8), b, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(barS);
+          umma_commit(&emptyK[s]);
         }
-        umma_commit(barPV);
-        umma_commit(&emptyV[s]);
-        return true;
-      };
-      for (int j = 0; ok && j < nb; j++) {
-        const int s = j % kStagesP;
-        // S_j overwrites the S buffer: the softmax warps must have loaded S_{j-1}.
-        if (j > 0 && !wait_or_abort(barSfree, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
-        if (!wait_or_abort(&fullK[s], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
-        tc_fence_after();
-        const uint64_t dk = dk0 + (uint64_t)((s * C::KV_BYTES) >> 4);
+      } else {
+        constexpr uint32_t idesc_pv = f16_idesc(HD, true);
+        constexpr uint32_t idesc_l = f16_idesc(16, false);
+        const uint64_t ones = noswz_desc(sbase + C::OFF_ONES, 128, 256);
+        // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK apart
+        // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
+        const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
+        for (int i = 0; i < nb; i++) {
+          const int s = i % kStagesP;
+          if (!wait_or_abort(&fullV[s], (uint32_t)(i / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+          // O and l rescaled for block i (after PV_{i-1}, which the correction warps waited for)
+          if (!wait_or_abort(&barCorr[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+          if (!wait_or_abort(barP, (uint32_t)i & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+          tc_fence_after();
+          const uint64_t dv = dv0 + (uint64_t)((s * C::KV_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++) {
-          // K step kk: Q columns kk*8.. (16 dims as f16 pairs); K chunk kk/4, 32 bytes per step
-          const uint64_t b = dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4);
-          umma_f16_ts(tmem + C::COL_S, tmem + C::COL_Q + (uint32_t)(kk * 8), b, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(barS);
-        umma_commit(&emptyK[s]);
-        if (j > 0 && !issue_pv(j - 1)) {
-          ok = false;
-          break;
+          for (int kk = 0; kk < kKeys / 16; kk++) {
+            const uint32_t a = tmem + C::COL_P + (uint32_t)(kk * 8);  // 16 keys = 8 columns of f16 pairs
+            umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tmem + C::COL_L, a, ones, idesc_l, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(barPV);
+          umma_commit(&emptyV[s]);
         }
       }
-      if (ok) (void)issue_pv(nb - 1);
       // No MMA may still be running when TMEM is freed, also after an abort (bounded wait).
-      umma_commit(barEnd);
-      (void)g4a::mbar_wait_bounded(barEnd, 0, p.err, G4A_DEVERR_WAIT_MMA);
+      umma_commit(my_end);
+      (void)g4a::mbar_wait_bounded(my_end, 0, p.err, G4A_DEVERR_WAIT_MMA);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------------ Q load, softmax, epilogue
     const int quarter = warp & 3;                               // TMEM lane quarter of this warp
     const int half = (warp - 4) >> 2;                           // keys [32*half, 32*half + 32) of a block
@@ -387,6 +405,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (lane == 0) g4a::mbar_arrive(barQ);
     }
     const float c2 = p.scale_log2;
+    float* alpha_buf = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
+    int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
     float m = -INFINITY;
     bool ok = true;
     for (int j = 0; j < nb; j++) {
@@ -400,67 +420,77 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       __syncwarp();
       if (lane == 0) g4a::mbar_arrive(barSfree);  // the S buffer may be overwritten now
       const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys + 32u * half;
-      const bool whole = key0 >= lo && key0 + 32u <= hi;
-      // scaled scores x = s * scale * log2(e); masked keys -inf
+      // Interior blocks (every key visible to every row of the warp) skip the mask.
+      const bool interior = __all_sync(0xffffffffu, key0 >= lo && key0 + 32u <= hi) && c2 > 0.f;
       float x[32];
+      float mx;
+      if (interior) {  // raw scores; max scales with c2 > 0
 #pragma unroll
-      for (int c = 0; c < 32; c++) {
-        float v = __uint_as_float(sv[c]) * c2;
-        if (!whole && !(key0 + (uint32_t)c >= lo && key0 + (uint32_t)c < hi)) v = -INFINITY;
-        x[c] = v;
-      }
-      float mq[4];
+        for (int c = 0; c < 32; c++) x[c] = __uint_as_float(sv[c]);
+      } else {
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        mq[q] = fmaxf(fmaxf(x[q], x[q + 4]), fmaxf(x[q + 8], x[q + 12]));
-        mq[q] = fmaxf(mq[q], fmaxf(fmaxf(x[q + 16], x[q + 20]), fmaxf(x[q + 24], x[q + 28])));
+        for (int c = 0; c < 32; c++) {
+          float v = __uint_as_float(sv[c]) * c2;
+          if (!(key0 + (uint32_t)c >= lo && key0 + (uint32_t)c < hi)) v = -INFINITY;
+          x[c] = v;
+        }
       }
-      float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      {
+        float mq[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          mq[q] = fmaxf(fmaxf(x[q], x[q + 4]), fmaxf(x[q + 8], x[q + 12]));
+          mq[q] = fmaxf(mq[q], fmaxf(fmaxf(x[q + 16], x[q + 20]), fmaxf(x[q + 24], x[q + 28])));
+        }
+        mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        if (interior) mx *= c2;
+      }
       // the row's other half (warp w +- 4, same lanes): exchange through shared memory
       red[half * kRows + r] = mx;
       g4a::named_bar_sync(1 + quarter, 64);
       mx = fmaxf(mx, red[(half ^ 1) * kRows + r]);
       g4a::named_bar_sync(1 + quarter, 64);  // both read before either writes the next block's max
-      // lazy rescale: only when the row max grows by more than 2^kRescaleP
+      // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx : m;
-      const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
-      const bool warp_rescale = __any_sync(0xffffffffu, grow && m != -INFINITY) && j > 0;
+      if (half == 0) {  // publish the row's factor for the correction warps (both halves agree)
+        const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
+        const bool need = __any_sync(0xffffffffu, grow && m != -INFINITY);
+        alpha_buf[(j & 1) * kRows + r] = alpha;
+        if (lane == 0) flag_buf[(j & 1) * 4 + quarter] = need ? 1 : 0;
+        __syncwarp();
+        if (lane == 0) g4a::mbar_arrive(&barAlpha[j & 1]);
+      }
       m = m_new;
       // P = 2^(x - m) rounded to f16 pairs (computed before waiting for the previous PV)
       uint32_t pw[16];
+      if (m == -INFINITY) {  // no visible key yet in this row
 #pragma unroll
-      for (int e = 0; e < 16; e++) {
-        const float a = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[2 * e] - m);
-        const float b = (m == -INFINITY) ? 0.f : g4a::fast_exp2(x[2 * e + 1] - m);
-        const __half2 h = __floats2half2_rn(a, b);
-        pw[e] = *reinterpret_cast<const uint32_t*>(&h);
+        for (int e = 0; e < 16; e++) pw[e] = 0u;
+      } else if (interior) {
+        const float nm = -m;
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const float a = g4a::fast_exp2(fmaf(x[2 * e], c2, nm));
+          const float b = g4a::fast_exp2(fmaf(x[2 * e + 1], c2, nm));
+          const __half2 h = __floats2half2_rn(a, b);
+          pw[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const float a = g4a::fast_exp2(x[2 * e] - m);
+          const float b = g4a::fast_exp2(x[2 * e + 1] - m);
+          const __half2 h = __floats2half2_rn(a, b);
+          pw[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
       }
-      // P and the O/l rescale both wait for PV_{j-1} (single P buffer; O holds PV_0 .. PV_{j-1}).
+      // single P buffer: PV_{j-1} must have read P_{j-1}
       if (j > 0) {
         ok = __all_sync(0xffffffffu,
                         wait_or_abort(barPV, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA));
         if (!ok) break;
         tc_fence_after();
-      }
-      if (warp_rescale) {
-        // half 0: O columns [0, HD/2); half 1: [HD/2, HD) and the l columns
-#pragma unroll 1
-        for (int c = 0; c < HD / 64 + half; c++) {
-          const uint32_t col = (c < HD / 64) ? (uint32_t)(C::COL_O + half * (HD / 2) + c * 32) : C::COL_L;
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_addr + col, o);
-#pragma unroll
-          for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          if (c < HD / 64) {
-            tmem_st32(tmem + lane_addr + col, o);
-          } else {
-            uint32_t o16[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) o16[i] = o[i];
-            tmem_st16(tmem + lane_addr + col, o16);
-          }
-        }
       }
       tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(16 * half), pw);
       tmem_wait_st();
@@ -490,6 +520,54 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
                           __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
       }
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------------ O/l correction
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const float* alpha_buf = reinterpret_cast<const float*>(smem + C::OFF_ALPHA);
+    const volatile int* flag_buf = reinterpret_cast<const volatile int*>(smem + C::OFF_FLAG);
+    for (int j = 0; j < nb; j++) {
+      if (!__all_sync(0xffffffffu, wait_or_abort(&barAlpha[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err,
+                                                  G4A_DEVERR_WAIT_MMA)))
+        break;
+      // (block 0: the flag is clear, nothing has been accumulated yet)
+      const float alpha = alpha_buf[(j & 1) * kRows + r];
+      const bool need = flag_buf[(j & 1) * 4 + quarter] != 0;
+      if (need) {
+        // O and l hold PV_0 .. PV_{j-1}: wait for the last of them
+        if (!__all_sync(0xffffffffu, wait_or_abort(barPV, (uint32_t)(j - 1) & 1u, abort_flag, p.err,
+                                                   G4A_DEVERR_WAIT_MMA)))
+          break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c <= HD / 32; c++) {
+          const uint32_t col = (c < HD / 32) ? (uint32_t)(C::COL_O + c * 32) : C::COL_L;
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_addr + col, o);
+#pragma unroll
+          for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          if (c < HD / 32) {
+            tmem_st32(tmem + lane_addr + col, o);
+          } else {
+            uint32_t o16[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) o16[i] = o[i];
+            tmem_st16(tmem + lane_addr + col, o16);
+          }
+        }
+        tmem_wait_st();
+      }
+      // A warp with nothing to do could otherwise run two blocks ahead of a slower one and count
+      // its arrival into the slower one's phase: arrive only after the previous phase of this
+      // parity (block j-2) has completed.
+      if (j >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&barCorr[j & 1], (uint32_t)((j >> 1) - 1) & 1u, abort_flag,
+                                                            p.err, G4A_DEVERR_WAIT_MMA)))
+        break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(&barCorr[j & 1]);
     }
   }
   tc_fence_before();
