@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the prefill, batched-paged and split-KV 1M measurements")
     ap.add_argument("--ncu-case", type=int, default=0, metavar="L",
                     help="small profiling workload: two L-token caches, six decode_attn calls, no timing")
     return ap.parse_args()
@@ -401,6 +403,13 @@ def run_ours(args):
         "clocks": clocks,
         "e2e": e2e,
     }
+    if not args.no_extras:
+        # every rank takes part (the same collective steps in the same order on every rank)
+        line["batched_paged"] = run_batched(ctx, torch, rank, world, dist)
+        line["splitkv_1m"] = run_splitkv(ctx, torch, rank, world, dist)
+        pf = run_prefill(ctx, torch)
+        if rank == 0:
+            line["prefill"] = pf
     if rank == 0 and world == 1 and not args.no_sweep:
         line["sweep"] = run_sweep(ctx, torch, args)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -460,6 +469,194 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank):
             "us_per_layer": ms * 1e3 / calls, "layer_calls": calls,
             "path": "g4a_memcpy_h2d x3 + g4a_attn_decode_layer (q/k norm+RoPE, v_norm, store, attention) + "
                     "g4a_memcpy_d2h per layer call, pinned host buffers"}
+
+
+def _max_over_ranks(torch, dist, value: float) -> float:
+    if not dist:
+        return value
+    t = torch.tensor([value], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_batched(ctx, torch, rank, world, dist):
+    """64 sequences, L ~ U[1024, 32768] (seeded), 64-token pages in a seeded
+    random order; a step is one sliding layer (W 512) and one global layer per sequence.  The
+    sequences are sharded over ranks by LPT on their KV bytes, with no collective; the time is the
+    max over ranks.  Page contents are seeded N(0,1) f16 (the bandwidth does not depend on them)."""
+    import numpy as np
+
+    from g4attn import dist as gdist
+    from g4attn import synth
+
+    lengths = synth.batched_lengths(2, 64, 1024, 32768)
+    bins = gdist.lpt_shard(gdist.decode_cost_bytes(lengths) + gdist.decode_cost_bytes(lengths, window=512), world)
+    mine = np.array(sorted(bins[rank]), dtype=np.int64)
+    lens = lengths[mine].astype(np.int32)
+    B = len(lens)
+    total_bytes = sum(kv_bytes(int(L), 512) + kv_bytes(int(L)) for L in lengths)
+    res = {"config": "config[2]: B=64, L~U[1k,32k] seed 2, 64-token pages, sliding (W 512) + global layer",
+           "sequences_on_rank0": B}
+    if B == 0:
+        us = 0.0
+    else:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(40 + rank)
+        layers = []
+        for li in range(2):
+            table, npages = synth.page_assignment(7 + li + 100 * rank, lens, 64)
+            kp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+            vp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+            layers.append((kp, vp, torch.from_numpy(table).cuda(), npages))
+        q = torch.randn((B, NQH, HD), generator=g, device="cuda")
+        out = torch.empty((B, NQH, HD), device="cuda")
+        kvl = torch.from_numpy(lens).cuda()
+        ctx.reserve_workspace(B, HD, NQH)
+
+        def step():
+            for li, (kp, vp, table, npages) in enumerate(layers):
+                ctx.decode_attn_paged(q, kp, vp, table, kvl, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                                      page_size=64, sliding_window=512 if li == 0 else 0, host_kv_lens=lens)
+
+        for _ in range(3):
+            step()
+        ctx.sync()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        ctx.set_stream(s.cuda_stream)
+        with torch.cuda.stream(s):
+            gr.capture_begin()
+            step()
+            gr.capture_end()
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        n = 50
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        del gr, layers
+    if dist:
+        dist.barrier()
+    us = _max_over_ranks(torch, dist, us)
+    hbm, _, _ = peaks()
+    res.update({"us_per_step": us, "GB/s": total_bytes / (us * 1e-6) / 1e9 if us else None,
+                "bytes_per_step": total_bytes, "frac_of_measured_hbm_per_gpu":
+                    (total_bytes / (us * 1e-6) / 1e9) / world / hbm if us else None,
+                "sharding": f"LPT over {world} rank(s), no collective"})
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_splitkv(ctx, torch, rank, world, dist):
+    """BASELINE config[4]: one 1,048,576-token global-layer decode, KV split evenly over the ranks;
+    each rank computes its slice's partial (m, l, o), the 8,256-byte partials are all-gathered
+    with NCCL and merged on every rank.  One rank: a single decode over the whole cache."""
+    from g4attn import dist as gdist
+
+    L = 1 << 20
+    b, e = gdist.splitkv_ranges(L, world, 64)[rank]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(60 + rank)
+    kc = torch.randn((e - b, NKH, HD), generator=g, device="cuda").half()
+    vc = torch.randn((e - b, NKH, HD), generator=g, device="cuda").half()
+    q = torch.randn((NQH, HD), generator=g, device="cuda")
+    out = torch.empty((NQH, HD), device="cuda")
+    dec = gdist.SplitKVDecoder(ctx) if dist else None
+
+    def step():
+        if dec:
+            dec.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L)
+        else:
+            ctx.decode_attn(q, kc, vc, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    n = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    us = _max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1e3 / n)
+    total = kv_bytes(L)
+    hbm, _, _ = peaks()
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"config": "config[4]: kv_len 1,048,576, 8 q heads / 1 kv head, head_dim 256, KV split evenly",
+            "us_per_layer": us, "GB/s": total / (us * 1e-6) / 1e9,
+            "frac_of_measured_hbm_per_gpu": total / (us * 1e-6) / 1e9 / world / hbm,
+            "exchange": "NCCL all_gather of 8,256-byte partials + lse merge" if dist else "none (one rank)",
+            "timing": "eager calls, CUDA events, max over ranks"}
+
+
+def run_prefill(ctx, torch):
+    """T = 4096 prompt tokens, 8 q heads / 1 kv head, head_dim 256; the prep
+    kernel (q/k norm+RoPE, v_norm, f16 K/V store, q to f16) then the tcgen05 attention kernel, for
+    the causal (theta 1e6) and the sliding-window (W 512, theta 1e4) mask.  TFLOP/s counts only
+    unmasked (query, key) pairs, 4 * NQH * HD flops each."""
+    import numpy as np
+
+    from g4attn import synth
+
+    _, bf16, kind = peaks()
+    T = 4096
+    res = {"config": "config[3]: T=4096, 8 q heads / 1 kv head, head_dim 256, f16 q/K/V, f32 accumulate",
+           "peak_tflops": bf16, "peak_kind": kind}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    rng = np.random.default_rng(3)
+    qw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).cuda().view(torch.float16)
+    kw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).cuda().view(torch.float16)
+    q = torch.randn((T, NQH, HD), generator=g, device="cuda")
+    k = torch.randn((T, NKH, HD), generator=g, device="cuda")
+    v = torch.randn((T, NKH, HD), generator=g, device="cuda")
+    kc = torch.empty((T, NKH, HD), dtype=torch.float16, device="cuda")
+    vc = torch.empty_like(kc)
+    q16 = torch.empty((T, NQH, HD), dtype=torch.float16, device="cuda")
+    out = torch.empty((T, NQH, HD), device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, W, theta in (("causal", 0, 1e6), ("sliding_512", 512, 1e4)):
+        def prep():
+            ctx.prefill_qkv_prep(q, k, v, qw, kw, None, q16, kc, vc, T=T, start_pos=0, max_seq_len=T,
+                                 num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, eps=EPS, theta=theta)
+
+        def attn():
+            ctx.prefill_attn(q16, kc, vc, out, T=T, start_pos=0, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                             scale=1.0, sliding_window=W)
+
+        prep()
+        for _ in range(3):
+            attn()
+        torch.cuda.synchronize()
+        n = 30
+        torch.cuda._sleep(20_000_000)
+        e0.record()
+        for _ in range(n):
+            attn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        torch.cuda._sleep(20_000_000)
+        e0.record()
+        for _ in range(n):
+            prep()
+            attn()
+        e1.record()
+        torch.cuda.synchronize()
+        us_both = e0.elapsed_time(e1) * 1e3 / n
+        fl = synth.prefill_flops(T, W)
+        res[name] = {"attn_us": us, "tflops": fl / (us * 1e-6) / 1e12, "frac_of_peak": fl / (us * 1e-6) / 1e12 / bf16,
+                     "prep_plus_attn_us": us_both, "flops": fl}
+    return res
 
 
 def run_sweep(ctx, torch, args):

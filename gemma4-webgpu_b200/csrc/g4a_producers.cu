@@ -165,27 +165,85 @@ __global__ void __launch_bounds__(kWG) decode_prep_kernel(float* q, float* k, fl
   g4a::pdl_launch_dependents();
 }
 
-// Prefill input stage: grid (nqh + nkh, T).  Token i is at position start_pos + i and is stored
-// at cache row start_pos + i.  Inputs are left untouched.
-__global__ void __launch_bounds__(kWG) prefill_prep_kernel(const float* q, const float* k, const float* v,
-                                                            const __half* qw, const __half* kw,
-                                                            const __half* rope_freqs, __half* q16, __half* k_cache,
-                                                            __half* v_cache, int nqh, int nkh, int hd, float eps,
-                                                            uint32_t start_pos, float theta, uint32_t apply_div) {
-  __shared__ float xs[kMaxHeadDim];
-  __shared__ float red[kWG];
-  const int b = blockIdx.x;
-  const uint32_t i = blockIdx.y;
+// Prefill input stage: one CTA per token (grid T), one warp per head (q heads, then k heads,
+// then v heads).  Token i is at position start_pos + i and is stored at cache row start_pos + i;
+// inputs are left untouched.  The RoPE sin/cos of the position are computed once per token.  A
+// warp reproduces the 256-thread WGSL sum-of-squares tree exactly: lane l holds elements
+// l + 32j, so thread t = l + 32j's partial sum (its elements t, t + 256, ... added from 0 in
+// order) and the first three halving levels (128, 64, 32) are lane-local adds in the same order,
+// and the last five levels are the same shuffles as in wg_tree_sum.  RoPE pairs (p, p + hd/2) are
+// lane-local too.  Every output is bit-identical to the single-head kernels.  head_dim must be
+// a multiple of 64 and at most 512.
+constexpr int kPrepMaxHd = 512;
+constexpr int kPrepMaxWarps = 32;
+
+__global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, const float* k, const float* v,
+                                                             const __half* qw, const __half* kw,
+                                                             const __half* rope_freqs, __half* q16, __half* k_cache,
+                                                             __half* v_cache, int nqh, int nkh, int hd, float eps,
+                                                             uint32_t start_pos, float theta, uint32_t apply_div) {
+  __shared__ float sn[kPrepMaxHd / 2], cs[kPrepMaxHd / 2];
+  const int t = threadIdx.x, lane = t & 31;
+  const uint32_t i = blockIdx.x;
   const uint32_t pos = start_pos + i;
-  if (b < nqh) {
-    const size_t off = ((size_t)i * nqh + b) * hd;
-    norm_rope_head(q + off, nullptr, q16 + off, qw, rope_freqs, hd, eps, pos, theta, apply_div, xs, red);
-  } else {
-    const int j = b - nqh;
-    const size_t in_off = ((size_t)i * nkh + j) * hd;
-    const size_t row = ((size_t)pos * nkh + j) * hd;
-    norm_rope_head(k + in_off, nullptr, k_cache + row, kw, rope_freqs, hd, eps, pos, theta, apply_div, xs, red);
-    vnorm_head(v + in_off, nullptr, v_cache + row, hd, eps, true, xs, red);
+  const int half_dim = hd / 2;
+  const float posf = __uint2float_rn(pos);
+  for (int p = t; p < half_dim; p += blockDim.x) {
+    const float angle = __fmul_rn(posf, rope_freq(p, hd, theta, rope_freqs, apply_div));
+    double s_, c_;
+    sincos((double)angle, &s_, &c_);
+    sn[p] = __double2float_rn(s_);
+    cs[p] = __double2float_rn(c_);
+  }
+  __syncthreads();
+  const int H = nqh + 2 * nkh;
+  const int nj = hd / 32;  // elements per lane (2..16)
+  for (int h = t >> 5; h < H; h += blockDim.x >> 5) {
+    const bool is_q = h < nqh, is_k = !is_q && h < nqh + nkh;
+    const float* src = is_q ? q + ((size_t)i * nqh + h) * hd
+                       : is_k ? k + ((size_t)i * nkh + (h - nqh)) * hd
+                              : v + ((size_t)i * nkh + (h - nqh - nkh)) * hd;
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) x[j] = (j < nj) ? src[lane + 32 * j] : 0.f;
+    // thread t = lane + 32j of the WGSL workgroup: partial over elements t, t + 256
+    float s8[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      float part = __fmul_rn(x[j], x[j]);  // 0 + x*x
+      if (j + 8 < nj) part = __fadd_rn(part, __fmul_rn(x[j + 8], x[j + 8]));
+      s8[j] = (j < nj) ? part : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) s8[j] = __fadd_rn(s8[j], s8[j + 4]);  // stride 128
+#pragma unroll
+    for (int j = 0; j < 2; j++) s8[j] = __fadd_rn(s8[j], s8[j + 2]);  // stride 64
+    float val = __fadd_rn(s8[0], s8[1]);                              // stride 32
+#pragma unroll
+    for (int stride = 16; stride >= 1; stride >>= 1) val = __fadd_rn(val, __shfl_down_sync(0xffffffffu, val, stride));
+    const float ss = __shfl_sync(0xffffffffu, val, 0);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
+    __half* dst;
+    if (is_q || is_k) {
+      const __half* w = is_q ? qw : kw;
+      dst = is_q ? q16 + ((size_t)i * nqh + h) * hd : k_cache + ((size_t)pos * nkh + (h - nqh)) * hd;
+      const int pj = nj / 2;  // pair partner of element j is j + pj
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (j < pj) {
+          const int p = lane + 32 * j;
+          const float x0 = __fdiv_rn(__fmul_rn(x[j], __half2float(w[p])), rms);
+          const float x1 = __fdiv_rn(__fmul_rn(x[j + pj], __half2float(w[p + half_dim])), rms);
+          dst[p] = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p])));
+          dst[p + half_dim] = __float2half_rn(__fadd_rn(__fmul_rn(x0, sn[p]), __fmul_rn(x1, cs[p])));
+        }
+      }
+    } else {
+      dst = v_cache + ((size_t)pos * nkh + (h - nqh - nkh)) * hd;
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        if (j < nj) dst[lane + 32 * j] = __float2half_rn(__fdiv_rn(x[j], rms));
+    }
   }
   g4a::pdl_launch_dependents();
 }
@@ -256,10 +314,15 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
   if ((uint64_t)start_pos + T > max_seq_len)
     return g4a_fail(G4A_EINVAL, "g4a_prefill_qkv_prep: start_pos %u + T %u exceeds max_seq_len %u", start_pos, T,
                     max_seq_len);
-  if (T > 65535u) return g4a_fail(G4A_EINVAL, "g4a_prefill_qkv_prep: T %u > 65535 per call", T);
-  dim3 grid(num_q_heads + num_kv_heads, T);
+  if (head_dim > (uint32_t)kPrepMaxHd || (head_dim % 64) != 0)
+    return g4a_fail(G4A_EINVAL, "g4a_prefill_qkv_prep: head_dim %u must be a multiple of 64 and <= %d", head_dim,
+                    kPrepMaxHd);
+  const uint32_t heads = num_q_heads + 2 * num_kv_heads;
+  if (heads == 0) return G4A_OK;
+  const uint32_t warps = heads < (uint32_t)kPrepMaxWarps ? heads : (uint32_t)kPrepMaxWarps;
+  dim3 grid(T);
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_PREP);
-  prefill_prep_kernel<<<grid, kWG, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
+  prefill_prep_kernel<<<grid, warps * 32, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
                                                      (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
                                                      (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads,
                                                      (int)head_dim, eps, start_pos, theta, apply_divisor);

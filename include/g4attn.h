@@ -219,7 +219,7 @@ g4a_status g4a_attn_decode_layer(g4a_ctx* ctx, float* q, float* k, float* v,
  * launch: q rows get norm+RoPE and are written as f16 to q16_out [T, num_q_heads, head_dim];
  * k rows get norm+RoPE, v rows the weightless v_norm, and both are stored as f16 into the
  * cache rows start_pos+i (cache slot = position).  q, k, v are f32 [T, heads, head_dim] and are
- * left unmodified.  start_pos + T must be <= max_seq_len. */
+ * left unmodified.  start_pos + T must be <= max_seq_len; head_dim a multiple of 64, <= 512. */
 g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, const float* v,
                                 const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                                 const uint16_t* rope_freqs, uint16_t* q16_out,

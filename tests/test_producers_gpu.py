@@ -113,3 +113,17 @@ def test_gpu_cache_builder_matches_oracle(ctx, oracle):
     kc, vc = gpu_build_cache(ctx, raw.k, raw.v, raw.k_w, theta=1e4)
     kref, vref = oracle.build_cache(raw.k, raw.v, raw.k_w, theta=1e4)
     assert same_bits(host(kc), kref) and same_bits(host(vc), vref)
+
+
+def test_prefill_prep_rejects_head_dim_off_the_warp_layout(ctx):
+    """The prefill input stage takes head_dim in multiples of 64 (<= 512); others fail on the host."""
+    from g4attn import G4AError
+
+    T, hd = 4, 96
+    f = torch.zeros((T, 1, hd), device="cuda")
+    h = torch.zeros((T, 1, hd), dtype=torch.float16, device="cuda")
+    w = torch.ones(hd, dtype=torch.float16, device="cuda")
+    with pytest.raises(G4AError) as ei:
+        ctx.prefill_qkv_prep(f, f, f, w, w, None, h, h, h, T=T, start_pos=0, max_seq_len=T, num_q_heads=1,
+                             num_kv_heads=1, head_dim=hd, eps=EPS, theta=1e4)
+    assert "multiple of 64" in str(ei.value)
