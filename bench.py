@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ncu-prefill", type=int, default=-1, metavar="W",
+                    help="small profiling workload: config[3] prefill with sliding window W (0 = causal), "
+                         "three launches, no timing")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the prefill, batched-paged and split-KV 1M measurements")
     ap.add_argument("--ncu-case", type=int, default=0, metavar="L",
@@ -377,7 +380,7 @@ def run_ours(args):
     launches_per_layer = (1 if k_n else 0) + (1 if m_n else 0)
 
     # ---- end to end through the C ABI with pinned host buffers
-    e2e = run_e2e(ctx, torch, kcs, vcs, L, R, min(args.steps * R, 4000), rank)
+    e2e = run_e2e(ctx, torch, kcs, vcs, L, R, min(args.steps * R, 4000), rank, world, dist)
 
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -425,9 +428,10 @@ def run_ours(args):
     return 0
 
 
-def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank):
+def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
     """The reference-facing path: pinned host q/k/v in, g4a_attn_decode_layer (producers +
-    attention), host out back, for every layer call, through the raw C ABI."""
+    attention), host out back, for every layer call, through the raw C ABI.  Every rank runs its
+    own calls; the value is the whole job's bytes over the slowest rank's device time."""
     import numpy as np
 
     from g4attn import _ptr
@@ -435,20 +439,18 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank):
 
     dev = torch.device("cuda", ctx.device)
     rng = np.random.default_rng(100 + rank)
-    hq = torch.from_numpy(rng.standard_normal((NQH, HD)).astype(np.float32)).pin_memory()
-    hk = torch.from_numpy(rng.standard_normal((NKH, HD)).astype(np.float32)).pin_memory()
-    hv = torch.from_numpy(rng.standard_normal((NKH, HD)).astype(np.float32)).pin_memory()
+    # q | k | v of a token in one pinned host buffer, copied with one call
+    hqkv = torch.from_numpy(rng.standard_normal((NQH + 2 * NKH) * HD).astype(np.float32)).pin_memory()
     hout = torch.zeros((NQH, HD), dtype=torch.float32).pin_memory()
-    q, k, v = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
+    qkv = torch.empty_like(hqkv, device=dev)
+    q, k, v = qkv[:NQH * HD], qkv[NQH * HD:(NQH + NKH) * HD], qkv[(NQH + NKH) * HD:]
     out = torch.empty((NQH, HD), device=dev)
     w = torch.ones(HD, dtype=torch.float16, device=dev)
     h = ctx.handle
     nb = lambda t: t.numel() * t.element_size()  # noqa: E731
 
     def layer_call(r):
-        call("g4a_memcpy_h2d", h, _ptr(q), _ptr(hq.data_ptr()), nb(hq))
-        call("g4a_memcpy_h2d", h, _ptr(k), _ptr(hk.data_ptr()), nb(hk))
-        call("g4a_memcpy_h2d", h, _ptr(v), _ptr(hv.data_ptr()), nb(hv))
+        call("g4a_memcpy_h2d", h, _ptr(qkv), _ptr(hqkv.data_ptr()), nb(hqkv))
         call("g4a_attn_decode_layer", h, _ptr(q), _ptr(k), _ptr(v), _ptr(w), _ptr(w), _ptr(None), _ptr(kcs[r]),
              _ptr(vcs[r]), _ptr(out), NQH, NKH, HD, EPS, L - 1, L - 1, L, L, 1e6, 0, 1.0, 0, 1)
         call("g4a_memcpy_d2h", h, _ptr(hout.data_ptr()), _ptr(out), nb(out))
@@ -456,19 +458,21 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank):
     for i in range(min(R, 8)):
         layer_call(i % R)
     ctx.sync()
+    if dist:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(calls):
         layer_call(i % R)
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+    ms = _max_over_ranks(torch, dist, e0.elapsed_time(e1))
     assert np.isfinite(hout.numpy()).all()
-    return {"value": kv_bytes(L) * calls / (ms / 1e3) / 1e9, "unit": "GB/s",
-            "h2d_bytes_per_step": nb(hq) + nb(hk) + nb(hv), "d2h_bytes_per_step": nb(hout),
-            "us_per_layer": ms * 1e3 / calls, "layer_calls": calls,
-            "path": "g4a_memcpy_h2d x3 + g4a_attn_decode_layer (q/k norm+RoPE, v_norm, store, attention) + "
-                    "g4a_memcpy_d2h per layer call, pinned host buffers"}
+    return {"value": kv_bytes(L) * calls * world / (ms / 1e3) / 1e9, "unit": "GB/s",
+            "h2d_bytes_per_step": nb(hqkv), "d2h_bytes_per_step": nb(hout),
+            "us_per_layer": ms * 1e3 / calls, "layer_calls_per_rank": calls,
+            "path": "g4a_memcpy_h2d of q|k|v + g4a_attn_decode_layer (q/k norm+RoPE, v_norm, store, attention) + "
+                    "g4a_memcpy_d2h of the output, per layer call, pinned host buffers"}
 
 
 def _max_over_ranks(torch, dist, value: float) -> float:
@@ -701,8 +705,42 @@ def run_ncu_case(L: int) -> int:
     return 0
 
 
+def run_ncu_prefill(W: int) -> int:
+    """Prep + three prefill-attention launches of config[3] (T = 4096), for ncu captures."""
+    import numpy as np
+    import torch
+
+    import g4attn
+    from g4attn import synth
+
+    T = 4096
+    with g4attn.Context(0) as ctx:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(3)
+        rng = np.random.default_rng(3)
+        qw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).cuda().view(torch.float16)
+        kw = torch.from_numpy(synth.norm_weight(rng, HD).view(np.uint16)).cuda().view(torch.float16)
+        q = torch.randn((T, NQH, HD), generator=g, device="cuda")
+        k = torch.randn((T, NKH, HD), generator=g, device="cuda")
+        v = torch.randn((T, NKH, HD), generator=g, device="cuda")
+        kc = torch.empty((T, NKH, HD), dtype=torch.float16, device="cuda")
+        vc = torch.empty_like(kc)
+        q16 = torch.empty((T, NQH, HD), dtype=torch.float16, device="cuda")
+        out = torch.empty((T, NQH, HD), device="cuda")
+        ctx.prefill_qkv_prep(q, k, v, qw, kw, None, q16, kc, vc, T=T, start_pos=0, max_seq_len=T, num_q_heads=NQH,
+                             num_kv_heads=NKH, head_dim=HD, eps=EPS, theta=1e6 if W == 0 else 1e4)
+        for _ in range(3):
+            ctx.prefill_attn(q16, kc, vc, out, T=T, start_pos=0, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                             sliding_window=W)
+        ctx.sync()
+        print(json.dumps({"ncu_prefill": W, "out_abs_sum": float(out.abs().sum())}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.ncu_prefill >= 0:
+        return run_ncu_prefill(args.ncu_prefill)
     if args.ncu_case:
         return run_ncu_case(args.ncu_case)
     if args.impl == "reference":
