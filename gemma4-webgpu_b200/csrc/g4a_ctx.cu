@@ -239,9 +239,10 @@ g4a_status g4a_sync(g4a_ctx* ctx, uint32_t timeout_ms) {
   if (derr != 0) {
     *ctx->dev_err_host = 0;
     return g4a_fail(G4A_ETIMEOUT, "g4a_sync: a kernel reported device error code %d (%s)", derr,
-                    derr == G4A_DEVERR_PAGE    ? "page id out of range, row skipped"
-                    : derr == G4A_DEVERR_KVLEN ? "kv_len beyond page-table capacity, capped"
-                                               : "bounded wait gave up");
+                    derr == G4A_DEVERR_PAGE        ? "page id out of range, row skipped"
+                    : derr == G4A_DEVERR_KVLEN     ? "kv_len beyond page-table capacity, capped"
+                    : derr == G4A_DEVERR_WAIT_PEER ? "a peer's split-KV partial did not arrive, output zeroed"
+                                                   : "bounded wait gave up");
   }
   return G4A_OK;
 }

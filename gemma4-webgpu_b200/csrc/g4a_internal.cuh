@@ -95,6 +95,7 @@ enum : int {
   G4A_DEVERR_WAIT_EMPTY = 2,  // producer gave up waiting for a free stage
   G4A_DEVERR_WAIT_MMA = 3,    // tensor-core completion wait gave up
   G4A_DEVERR_TMEM = 4,        // TMEM allocation failed / inconsistent
+  G4A_DEVERR_WAIT_PEER = 5,   // a peer's exchange flag did not arrive in time
   G4A_DEVERR_KVLEN = 16,      // kv_lens[b] exceeded the page table's capacity (capped)
   G4A_DEVERR_PAGE = 17,       // page id out of [0, num_pages) (row skipped)
 };

@@ -231,6 +231,45 @@ class Context:
              float(eps), int(position), int(slot), int(kv_len), int(max_seq_len), float(theta),
              int(apply_divisor), float(scale), int(sliding_window), int(is_producer))
 
+    # ---------------------------------------------------------------- memory and IPC
+    def alloc(self, nbytes: int) -> int:
+        """Device allocation through the library (cudaMalloc); returns the address."""
+        p = c_void_p()
+        call("g4a_alloc", self._h, int(nbytes), ctypes.byref(p))
+        return int(p.value or 0)
+
+    def free(self, dptr: int) -> None:
+        call("g4a_free", self._h, c_void_p(dptr))
+
+    def memset(self, dptr: int, value: int, nbytes: int) -> None:
+        call("g4a_memset", self._h, c_void_p(dptr), int(value), int(nbytes))
+
+    def ipc_handle(self, dptr: int) -> bytes:
+        buf = (ctypes.c_uint8 * 64)()
+        call("g4a_ipc_get_handle", self._h, c_void_p(dptr), ctypes.cast(buf, c_void_p))
+        return bytes(buf)
+
+    def ipc_open(self, handle: bytes) -> int:
+        buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+        p = c_void_p()
+        call("g4a_ipc_open_handle", self._h, ctypes.cast(buf, c_void_p), ctypes.byref(p))
+        return int(p.value or 0)
+
+    def ipc_close(self, dptr: int) -> None:
+        call("g4a_ipc_close_handle", self._h, c_void_p(dptr))
+
+    def splitkv_exchange_merge(self, part, rank_buffers: list[int], rank: int, seq: int, out, *, num_q_heads,
+                               head_dim) -> None:
+        """Push this rank's partial to every rank over peer memory, wait for all, merge (see the
+        C header for the protocol)."""
+        import torch
+
+        _check(part, "part", torch.float32, num_q_heads * (head_dim + 2), self.device)
+        _check(out, "out", torch.float32, num_q_heads * head_dim, self.device)
+        arr = (c_void_p * len(rank_buffers))(*[c_void_p(b) for b in rank_buffers])
+        call("g4a_splitkv_exchange_merge", self._h, _ptr(part), arr, len(rank_buffers), int(rank), int(seq),
+             num_q_heads, head_dim, _ptr(out))
+
     # ---------------------------------------------------------------- prefill
     def prefill_qkv_prep(self, q, k, v, q_norm_w, k_norm_w, rope_freqs, q16_out, k_cache, v_cache, *, T,
                          start_pos, max_seq_len, num_q_heads, num_kv_heads, head_dim, eps, theta,

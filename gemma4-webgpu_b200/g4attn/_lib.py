@@ -67,9 +67,14 @@ SIGNATURES: dict[str, list] = {
     "g4a_prefill_qkv_prep": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f,
                              _u32],
     "g4a_prefill_attn": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _f, _u32],
+    "g4a_ipc_get_handle": [_p, _p, _p],
+    "g4a_ipc_open_handle": [_p, _p, POINTER(c_void_p)],
+    "g4a_ipc_close_handle": [_p, _p],
+    "g4a_splitkv_exchange_merge": [_p, _p, POINTER(c_void_p), _u32, _u32, _u32, _u32, _u32, _p],
 }
 EXTRA_SYMBOLS = {"g4a_last_error": ([], c_char_p), "g4a_version": ([], c_char_p),
-                 "g4a_get_stream": ([c_void_p], c_void_p)}
+                 "g4a_get_stream": ([c_void_p], c_void_p),
+                 "g4a_exchange_buffer_bytes": ([c_uint32, c_uint32, c_uint32], c_size_t)}
 
 _lib = None
 

@@ -114,3 +114,74 @@ class SplitKVDecoder:
         self.partial(q, k_slice, v_slice, begin=begin, end=end, kv_len_total=kv_len_total, scale=scale,
                      sliding_window=sliding_window)
         return self.gather_and_merge(out)
+
+
+class PeerSplitKVDecoder:
+    """Long-context decode of one sequence split along KV length, with the partials exchanged
+    over NVLink peer memory by the library's exchange kernel instead of a collective.
+
+    Every rank allocates one exchange buffer (``g4a_exchange_buffer_bytes``), exports it as a
+    CUDA IPC handle, and opens the other ranks' handles; the 64-byte handles travel once over
+    the process group (any backend).  ``step`` computes this rank's partial and calls
+    ``splitkv_exchange_merge``, which pushes it into every rank's buffer, waits for all of them
+    and merges; every rank ends with the full attention output.  All ranks must call ``step``
+    the same number of times; ``close`` (collective) releases the buffers after a barrier.
+    """
+
+    def __init__(self, ctx, group=None, num_q_heads: int = 8, head_dim: int = 256):
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import load
+
+        self.ctx = ctx
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nqh = num_q_heads
+        self.hd = head_dim
+        self.seq = 0
+        nbytes = int(load().g4a_exchange_buffer_bytes(self.world, num_q_heads, head_dim))
+        self.own = ctx.alloc(nbytes)
+        ctx.memset(self.own, 0, nbytes)
+        ctx.sync()
+        handle = torch.tensor(list(ctx.ipc_handle(self.own)), dtype=torch.uint8)
+        if dist.get_backend(group) == "nccl":
+            handle = handle.cuda(ctx.device)
+        handles = [torch.zeros_like(handle) for _ in range(self.world)]
+        dist.all_gather(handles, handle, group=group)
+        self.opened = []
+        self.buffers = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.buffers.append(self.own)
+            else:
+                p = ctx.ipc_open(bytes(h.cpu().tolist()))
+                self.opened.append(p)
+                self.buffers.append(p)
+        dist.barrier(group=group)
+        dev = torch.device("cuda", ctx.device)
+        self.part = torch.empty(partial_floats(num_q_heads, head_dim), dtype=torch.float32, device=dev)
+
+    def step(self, q, k_slice, v_slice, out, *, begin, end, kv_len_total, scale=1.0, sliding_window=0,
+             num_kv_heads=1):
+        self.ctx.decode_attn_partial(q, k_slice, v_slice, self.part, num_q_heads=self.nqh, num_kv_heads=num_kv_heads,
+                                     head_dim=self.hd, kv_begin=begin, kv_end=end, kv_len_total=kv_len_total,
+                                     scale=scale, sliding_window=sliding_window)
+        self.seq += 1
+        self.ctx.splitkv_exchange_merge(self.part, self.buffers, self.rank, self.seq, out, num_q_heads=self.nqh,
+                                        head_dim=self.hd)
+        return out
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        self.ctx.sync()
+        dist.barrier(group=self.group)  # nobody writes into a buffer after this point
+        for p in self.opened:
+            self.ctx.ipc_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        if self.own:
+            self.ctx.free(self.own)
+            self.own = 0

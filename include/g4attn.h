@@ -240,6 +240,31 @@ g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k
                             uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
                             float scale, uint32_t sliding_window);
 
+/* ------------------------------------------------------------------ multi-GPU exchange */
+
+/* Split-KV decode over several GPUs with the partial exchange done over NVLink peer memory
+ * instead of a collective library call (no reference counterpart: the reference runs on one
+ * WebGPU device).  One process per GPU.  Each rank allocates one exchange buffer of
+ * g4a_exchange_buffer_bytes(world, num_q_heads, head_dim) bytes with g4a_alloc, zeroes it once
+ * with g4a_memset, exports it with g4a_ipc_get_handle, sends the handle to every other rank
+ * (e.g. over torch.distributed), and opens the others' handles with g4a_ipc_open_handle.
+ * Every step, every rank calls g4a_splitkv_exchange_merge with the same `seq` (1, 2, 3, ...):
+ * it stores this rank's partial (the m | l | o layout of g4a_decode_attn_partial) into slot
+ * `rank` of every rank's buffer, raises its flag there, waits until every rank's partial of
+ * this step is in its own buffer (2 s bound; then the output is zeroed and g4a_sync reports
+ * the error), and writes the merged attention output [num_q_heads, head_dim] to `out`.
+ * rank_buffers is a host array of `world` device pointers: this rank's own buffer at index
+ * `rank`, the opened peer buffers elsewhere.  1 <= world <= 8.  Before freeing a buffer, make
+ * sure no rank will write to it again (e.g. a barrier after the last step). */
+#define G4A_IPC_HANDLE_BYTES 64
+size_t g4a_exchange_buffer_bytes(uint32_t world, uint32_t num_q_heads, uint32_t head_dim);
+g4a_status g4a_ipc_get_handle(g4a_ctx* ctx, void* dptr, uint8_t* out_handle);
+g4a_status g4a_ipc_open_handle(g4a_ctx* ctx, const uint8_t* handle, void** out_dptr);
+g4a_status g4a_ipc_close_handle(g4a_ctx* ctx, void* dptr);
+g4a_status g4a_splitkv_exchange_merge(g4a_ctx* ctx, const float* part, void* const* rank_buffers,
+                                      uint32_t world, uint32_t rank, uint32_t seq,
+                                      uint32_t num_q_heads, uint32_t head_dim, float* out);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
