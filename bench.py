@@ -570,36 +570,44 @@ def run_splitkv(ctx, torch, rank, world, dist):
     vc = torch.randn((e - b, NKH, HD), generator=g, device="cuda").half()
     q = torch.randn((NQH, HD), generator=g, device="cuda")
     out = torch.empty((NQH, HD), device="cuda")
-    dec = gdist.SplitKVDecoder(ctx) if dist else None
 
-    def step():
-        if dec:
-            dec.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L)
-        else:
-            ctx.decode_attn(q, kc, vc, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+    def timed(step) -> float:
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        n = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        return _max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1e3 / n)
 
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    n = 20
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(n):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    us = _max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1e3 / n)
+    res = {"config": "config[4]: kv_len 1,048,576, 8 q heads / 1 kv head, head_dim 256, KV split evenly",
+           "timing": "eager calls, CUDA events, max over ranks"}
     total = kv_bytes(L)
     hbm, _, _ = peaks()
+    if dist:
+        # the library's exchange over NVLink peer memory (the product path) ...
+        peer = gdist.PeerSplitKVDecoder(ctx)
+        us = timed(lambda: peer.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L))
+        peer.close()
+        # ... and, for comparison, NCCL all_gather + the lse merge kernel
+        nccl = gdist.SplitKVDecoder(ctx)
+        res["nccl_allgather_us_per_layer"] = timed(lambda: nccl.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L))
+        res["exchange"] = "partials pushed to every rank over NVLink peer memory by one exchange+merge kernel"
+    else:
+        us = timed(lambda: ctx.decode_attn(q, kc, vc, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                                           seq_len=L))
+        res["exchange"] = "none (one rank)"
     del kc, vc
     torch.cuda.empty_cache()
-    return {"config": "config[4]: kv_len 1,048,576, 8 q heads / 1 kv head, head_dim 256, KV split evenly",
-            "us_per_layer": us, "GB/s": total / (us * 1e-6) / 1e9,
-            "frac_of_measured_hbm_per_gpu": total / (us * 1e-6) / 1e9 / world / hbm,
-            "exchange": "NCCL all_gather of 8,256-byte partials + lse merge" if dist else "none (one rank)",
-            "timing": "eager calls, CUDA events, max over ranks"}
+    res.update({"us_per_layer": us, "GB/s": total / (us * 1e-6) / 1e9,
+                "frac_of_measured_hbm_per_gpu": total / (us * 1e-6) / 1e9 / world / hbm})
+    return res
 
 
 def run_prefill(ctx, torch):

@@ -52,10 +52,12 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, 
     for (int i = tid; i < pf / 4; i += blockDim.x)
       reinterpret_cast<float4*>(slot)[i] = __ldcg(reinterpret_cast<const float4*>(part) + i);
     for (int i = (pf & ~3) + tid; i < pf; i += blockDim.x) slot[i] = __ldcg(part + i);
-    __threadfence_system();
+    // The CTA barrier orders every thread's stores before thread 0's system-scope fence, which
+    // makes them visible to the destination GPU before the release store of the flag.
     __syncthreads();
     if (tid == 0) {
       uint32_t* flags = reinterpret_cast<uint32_t*>(peers.buf[dst] + slots_floats);
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
       st_release_sys(flags + par * world + rank, seq);
     }
   }
@@ -65,14 +67,14 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, 
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.buf[rank] + slots_floats) + par * world;
     const uint64_t t0 = g4a::globaltimer_ns();
     int good = 1;
+    uint32_t spins = 0;
     for (int j = 0; j < world; j++) {
       while (ld_acquire_sys(flags + j) != seq) {
-        if (g4a::globaltimer_ns() - t0 > 2000000000ull) {
+        if ((++spins & 1023u) == 0u && g4a::globaltimer_ns() - t0 > 2000000000ull) {
           good = 0;
           if (err) atomicExch(err, G4A_DEVERR_WAIT_PEER);
           break;
         }
-        __nanosleep(64);
       }
       if (!good) break;
     }
