@@ -1,4 +1,4 @@
-// Prefill attention on the tensor cores (tcgen05.mma, TMEM operands and accumulators, TMA tile
+// Prefill attention on the tensor cores (tcgen05.mma, TMEM accumulators and operands, TMA tile
 // loads).
 //
 // The reference has no prefill attention kernel: prefillBatched (src/engine.ts:2460-2479) runs
@@ -9,30 +9,31 @@
 //
 // Tile: 128 query rows = 16 consecutive tokens x the 8 q heads that share one kv head (GQA 8:1),
 // so every row of a tile reads the same K/V rows.  One CTA per tile, heaviest (latest) tiles
-// first.  The MMAs are bound by shared-memory bandwidth (128 B/clk/SM) when both operands come
-// from shared memory, so the M-side operands live in TMEM: Q (loaded once) and P (each block),
-// and shared memory carries only the K and V blocks.  TMEM columns (HD 256): O [0, 256),
-// Q [256, 384) as f16 pairs, S [384, 448), P [448, 480) as f16 pairs, l [480, 496).
-// Warp roles (384 threads):
-//   warp 0 lane 0   TMA producer of K blocks (64 keys) into a 3-stage ring; a stage is released
-//                   as soon as S_j has been computed from it.
-//   warp 2 lane 0   TMA producer of V blocks into their own 3-stage ring (released after PV_j).
-//   warp 1          allocates TMEM; lane 0 issues the score MMAs S_j = Q K_j^T (M 128, N 64,
-//                   K = HD, f16 in / f32 accumulate, A from TMEM).
-//   warp 3 lane 0   issues O += P_j V_j (N = HD) and l += P_j x ones (N = 16), A = P from TMEM.
-//   warps 4-11      Q into TMEM at the start; then softmax, two threads per query row (TMEM
-//                   lane = row; warps w and w+4 take keys 0-31 and 32-63 of a block and exchange
-//                   row maxima through shared memory): scores from TMEM (the S buffer is handed
-//                   back right after the load), window/causal mask (boundary blocks only),
-//                   online softmax in base 2 with lazy rescaling (the running max is only raised
-//                   when a row's max grows by more than 2^8), P rounded to f16 into TMEM.  l is
-//                   accumulated by the tensor core from the same f16 P as the output, so
-//                   numerator and denominator use identical weights.  Epilogue: O / l from TMEM
-//                   to the f32 output.
+// first.  Q (one TMA load) and 2-stage rings of K and V blocks (64 keys per block, one TMA op
+// per tensor per block, 128-byte swizzle) live in shared memory.  TMEM (HD 256): O [0, 256),
+// l [256, 272), two score buffers S0/S1 [288, 416), two P buffers (f16 pairs) [416, 480).
+// Double-buffering S and P lets the score MMA of block j+1 and the softmax of block j overlap
+// the PV MMA of block j-1, and keeps the softmax off the O-correction chain.
+// Warp roles (512 threads):
+//   warp 0 lane 0   TMA: Q once, then K blocks (a K stage is released when S_j is done).
+//   warp 2 lane 0   TMA: V blocks (a V stage is released when PV_j is done).
+//   warp 1          allocates TMEM; lane 0 issues S_j = Q K_j^T (M 128, N 64, K = HD, f16 in /
+//                   f32 accumulate, both operands from shared memory) into S[j % 2].
+//   warp 3 lane 0   issues O += P_j V_j (N = HD) and l += P_j x ones (N = 16), A = P[j % 2] from
+//                   TMEM.
+//   warps 4-11      softmax, two threads per query row (TMEM lane = row; warps w and w+4 take
+//                   keys 0-31 and 32-63 of a block and exchange row maxima through shared
+//                   memory): scores from TMEM (handed back right after the load), window/causal
+//                   mask (boundary blocks only), online softmax in base 2 with lazy rescaling
+//                   (the running max is only raised when a row's max grows by more than 2^8),
+//                   P rounded to f16 into TMEM.  l is accumulated by the tensor core from the
+//                   same f16 P as the output, so numerator and denominator use identical
+//                   weights.  Epilogue: O / l from TMEM to the f32 output.
 //   warps 12-15     correction: when a row's running max was raised, scale its O and l in TMEM
-//                   by 2^(m_old - m_new) after PV_{j-1} and before PV_j, off the softmax path.
+//                   by 2^(m_old - m_new) after PV_{j-1} and before PV_j.
 // Every mbarrier wait is bounded; after a timeout the CTA records an error, stops waiting and
-// frees its TMEM.
+// frees its TMEM.  Barriers that complete once per block come in pairs (one per block parity)
+// wherever a consumer could otherwise fall two phases behind its producer.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -45,7 +46,7 @@ constexpr int kRows = 128;                 // query rows per tile (TMEM lanes)
 constexpr int kHeadsPerKv = 8;             // q heads per kv head handled by this kernel
 constexpr int kTokPerTile = kRows / kHeadsPerKv;
 constexpr int kKeys = 64;                  // keys per block
-constexpr int kStagesP = 3;                // K and V ring depth
+constexpr int kStagesP = 2;                // K and V ring depth
 constexpr int kThreadsP = 512;
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units)
@@ -53,31 +54,32 @@ constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units
 template <int HD>
 struct PCfg {
   static constexpr int NCB = HD / 64;               // 64-dim chunks (128-byte swizzle rows)
+  static constexpr int Q_CHUNK = kRows * 128;       // bytes of one chunk of the Q tile
   static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
+  static constexpr int Q_BYTES = NCB * Q_CHUNK;
   static constexpr int KV_BYTES = NCB * KV_CHUNK;
-  static constexpr int OFF_K = 0;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
   static constexpr int OFF_ONES = OFF_V + kStagesP * KV_BYTES;  // 512 B of f16 ones (l MMA operand)
   static constexpr int OFF_RED = OFF_ONES + 512;                // [2 halves][128 rows] row maxima
   static constexpr int OFF_ALPHA = OFF_RED + 2 * kRows * 4;     // [2 parities][128 rows] rescale factors
   static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
   static constexpr int OFF_BAR = OFF_FLAG + 64;
-  static constexpr int NBARS = 23;
+  static constexpr int NBARS = 24;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
-  // TMEM columns (32-bit each; f16 operands hold two elements per column)
+  // TMEM columns (32-bit each; P holds two f16 per column)
   static constexpr uint32_t COL_O = 0;
-  static constexpr uint32_t COL_Q = HD;
-  static constexpr uint32_t COL_S = HD + HD / 2;
-  static constexpr uint32_t COL_P = COL_S + kKeys;
-  static constexpr uint32_t COL_L = COL_P + kKeys / 2;
-  static constexpr uint32_t TMEM_COLS = (COL_L + 16) <= 256 ? 256u : 512u;
+  static constexpr uint32_t COL_L = HD;
+  static constexpr uint32_t COL_S = HD + 32;                     // S[b] at COL_S + 64 b
+  static constexpr uint32_t COL_P = COL_S + 2 * kKeys;           // P[b] at COL_P + 32 b
+  static constexpr uint32_t TMEM_COLS = (COL_P + kKeys) <= 256 ? 256u : 512u;
   static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte aligned operands");
-  static_assert(COL_L + 16 <= TMEM_COLS, "TMEM budget");
+  static_assert(COL_P + kKeys <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 struct PrefillParams {
-  const uint16_t* q16;   // [T, nqh, HD] f16
   float* out;            // [T, nqh, HD] f32
   int T;
   uint32_t start_pos;
@@ -209,32 +211,45 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   }
 }
 
+// D (+)= A B^T with both operands as shared-memory descriptors.
+__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Warp-uniform bounded wait (the tcgen05.ld/st after it are warp-collective).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag, err, G4A_DEVERR_WAIT_MMA));
+}
+
 // --------------------------------------------------------------------------- the kernel
 template <int HD>
 __global__ void __launch_bounds__(kThreadsP, 1)
-    prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                        const PrefillParams p) {
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
   using C = PCfg<HD>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* fullK = bars;           // [3] K block landed
-  uint64_t* fullV = bars + 3;       // [3] V block landed
-  uint64_t* emptyK = bars + 6;      // [3] K stage consumed by S_j (tcgen05.commit)
-  uint64_t* emptyV = bars + 9;      // [3] V stage consumed by PV_j (tcgen05.commit)
-  uint64_t* barQ = bars + 12;       // Q in TMEM (8 softmax warps)
-  uint64_t* barS = bars + 13;       // S_j in TMEM (tcgen05.commit), once per block
-  uint64_t* barSfree = bars + 14;   // S_j loaded by the softmax warps (8 warps), once per block
-  uint64_t* barP = bars + 15;       // P_j in TMEM, O/l rescaled (8 warps), once per block
-  uint64_t* barPV = bars + 16;      // PV_j and l_j done (tcgen05.commit), once per block
-  uint64_t* barEnd = bars + 17;     // every score MMA done (tcgen05.commit)
-  // One barrier per block parity: the correction of block j+1 may finish before the MMA thread
-  // waits for that of block j (and the factors of j+1 may be published before the correction
-  // warps wait for those of j), so a single barrier could complete twice between two waits.
-  uint64_t* barAlpha = bars + 18;   // [2] rescale factors of block j published (4 softmax warps)
-  uint64_t* barCorr = bars + 20;    // [2] O/l rescaled for block j (4 correction warps)
-  uint64_t* barEnd2 = bars + 22;    // every PV/l MMA done (tcgen05.commit)
+  uint64_t* fullK = bars;           // [2] K block landed
+  uint64_t* fullV = bars + 2;       // [2] V block landed
+  uint64_t* emptyK = bars + 4;      // [2] K stage consumed by S_j (tcgen05.commit)
+  uint64_t* emptyV = bars + 6;      // [2] V stage consumed by PV_j (tcgen05.commit)
+  uint64_t* barQ = bars + 8;        // Q tile landed
+  uint64_t* barS = bars + 9;        // [2] S_j in S[j % 2] (tcgen05.commit)
+  uint64_t* barSfree = bars + 11;   // [2] S_j loaded by the softmax warps (8 warps)
+  uint64_t* barP = bars + 13;       // [2] P_j in P[j % 2] (8 softmax warps)
+  uint64_t* barPV = bars + 15;      // [2] PV_j and l_j done (tcgen05.commit)
+  uint64_t* barEnd = bars + 17;     // every score MMA done
+  uint64_t* barEnd2 = bars + 18;    // every PV / l MMA done
+  uint64_t* barAlpha = bars + 19;   // [2] rescale factors of block j published (4 softmax warps)
+  uint64_t* barCorr = bars + 21;    // [2] O/l rescaled for block j (4 correction warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -249,25 +264,24 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const int nb = (int)((hi_max - 1u) / kKeys) - kb0 + 1;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStagesP; s++) {
+    for (int s = 0; s < 2; s++) {
       g4a::mbar_init(&fullK[s], 1);
       g4a::mbar_init(&fullV[s], 1);
       g4a::mbar_init(&emptyK[s], 1);
       g4a::mbar_init(&emptyV[s], 1);
-    }
-    g4a::mbar_init(barQ, 8);
-    g4a::mbar_init(barS, 1);
-    g4a::mbar_init(barSfree, 8);
-    g4a::mbar_init(barP, 8);
-    g4a::mbar_init(barPV, 1);
-    g4a::mbar_init(barEnd, 1);
-    g4a::mbar_init(barEnd2, 1);
-    for (int s = 0; s < 2; s++) {
+      g4a::mbar_init(&barS[s], 1);
+      g4a::mbar_init(&barSfree[s], 8);
+      g4a::mbar_init(&barP[s], 8);
+      g4a::mbar_init(&barPV[s], 1);
       g4a::mbar_init(&barAlpha[s], 4);
       g4a::mbar_init(&barCorr[s], 4);
     }
+    g4a::mbar_init(barQ, 1);
+    g4a::mbar_init(barEnd, 1);
+    g4a::mbar_init(barEnd2, 1);
     *abort_flag = 0;
     g4a::fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
@@ -296,51 +310,60 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const bool kside = warp == 0;
       uint64_t pol_kv;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_kv));
+      if (kside) {
+        uint64_t pol_q;
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_q));
+        g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_BYTES);
+        tma_load_4d_p(sbase + C::OFF_Q, &tmq, 0, kvh * kHeadsPerKv, t0, 0, barQ, pol_q);
+      }
       uint64_t* empty = kside ? emptyK : emptyV;
       uint64_t* full = kside ? fullK : fullV;
       const CUtensorMap* map = kside ? &tmk : &tmv;
       const uint32_t dst0 = sbase + (kside ? C::OFF_K : C::OFF_V);
       for (int j = 0; j < nb; j++) {
-        const int s = j % kStagesP;
-        if (j >= kStagesP && !wait_or_abort(&empty[s], (uint32_t)(j / kStagesP - 1) & 1u, abort_flag, p.err,
-                                            G4A_DEVERR_WAIT_EMPTY))
+        const int s = j & 1;
+        if (j >= 2 && !wait_or_abort(&empty[s], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
+                                     G4A_DEVERR_WAIT_EMPTY))
           break;
         g4a::mbar_arrive_expect_tx(&full[s], (uint32_t)C::KV_BYTES);
         tma_load_4d_p(dst0 + s * C::KV_BYTES, map, 0, kvh, (kb0 + j) * kKeys, 0, &full[s], pol_kv);
       }
       // Loads still in flight land before the CTA retires (bounded).
-      for (int j = max(0, nb - kStagesP); j < nb; j++)
-        (void)wait_or_abort(&full[j % kStagesP], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err,
-                            G4A_DEVERR_WAIT_FULL);
+      for (int j = max(0, nb - 2); j < nb; j++)
+        (void)wait_or_abort(&full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+      if (kside) (void)wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------ MMA issuers
     // Two issuing threads, so that the waits of one never leave the tensor pipe without work:
     // warp 1 issues the score MMAs, warp 3 the PV and l MMAs.  Each commit tracks the MMAs of its
-    // own thread.
+    // own thread.  Base descriptors are built once; a K step only adds a constant to the
+    // start-address field (bits 0-13, in 16-byte units; every operand lies below 256 KB).
     if (lane == 0) {
       uint64_t* my_end = (warp == 1) ? barEnd : barEnd2;
       if (warp == 1) {
         constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
-        // Base descriptor, built once; a K step only adds a constant to the start-address field
-        // (bits 0-13, in 16-byte units; every operand lies below 256 KB, so no carry leaves it).
+        const uint64_t dq = sw128_desc(sbase + C::OFF_Q, 16, 1024);
         const uint64_t dk0 = sw128_desc(sbase + C::OFF_K, 16, 1024);
-        bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_MMA);
+        bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
         for (int j = 0; ok && j < nb; j++) {
-          const int s = j % kStagesP;
-          // S_j overwrites the S buffer: the softmax warps must have loaded S_{j-1}.
-          if (j > 0 && !wait_or_abort(barSfree, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
-          if (!wait_or_abort(&fullK[s], (uint32_t)(j / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+          const int b = j & 1;
+          // S[b] was last read out by the softmax of block j-2
+          if (j >= 2 && !wait_or_abort(&barSfree[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
+                                       G4A_DEVERR_WAIT_MMA))
+            break;
+          if (!wait_or_abort(&fullK[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
           tc_fence_after();
-          const uint64_t dk = dk0 + (uint64_t)((s * C::KV_BYTES) >> 4);
+          const uint64_t dk = dk0 + (uint64_t)((b * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; kk++) {
-            // K step kk: Q columns kk*8.. (16 dims as f16 pairs); K chunk kk/4, 32 bytes per step
-            const uint64_t b = dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK + (kk & 3) * 32) >> 4);
-            umma_f16_ts(tmem + C::COL_S, tmem + C::COL_Q + (uint32_t)(kk * 8), b, idesc_s, kk > 0 ? 1u : 0u);
+            // K step kk: 64-dim chunk kk / 4, 32 bytes (16 dims) per step along the swizzled row
+            const uint64_t off = (uint64_t)(((kk & 3) * 32) >> 4);
+            umma_f16_ss(tmem + C::COL_S + (uint32_t)(b * kKeys), dq + (uint64_t)(((kk >> 2) * C::Q_CHUNK) >> 4) + off,
+                        dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK) >> 4) + off, idesc_s, kk > 0 ? 1u : 0u);
           }
-          umma_commit(barS);
-          umma_commit(&emptyK[s]);
+          umma_commit(&barS[b]);
+          umma_commit(&emptyK[b]);
         }
       } else {
         constexpr uint32_t idesc_pv = f16_idesc(HD, true);
@@ -350,21 +373,21 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
         const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
         for (int i = 0; i < nb; i++) {
-          const int s = i % kStagesP;
-          if (!wait_or_abort(&fullV[s], (uint32_t)(i / kStagesP) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
+          const int b = i & 1;
+          if (!wait_or_abort(&fullV[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
           // O and l rescaled for block i (after PV_{i-1}, which the correction warps waited for)
-          if (!wait_or_abort(&barCorr[i & 1], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
-          if (!wait_or_abort(barP, (uint32_t)i & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+          if (!wait_or_abort(&barCorr[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
+          if (!wait_or_abort(&barP[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
           tc_fence_after();
-          const uint64_t dv = dv0 + (uint64_t)((s * C::KV_BYTES) >> 4);
+          const uint64_t dv = dv0 + (uint64_t)((b * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; kk++) {
-            const uint32_t a = tmem + C::COL_P + (uint32_t)(kk * 8);  // 16 keys = 8 columns of f16 pairs
+            const uint32_t a = tmem + C::COL_P + (uint32_t)(b * (kKeys / 2) + kk * 8);  // 16 keys = 8 columns
             umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
             umma_f16_ts(tmem + C::COL_L, a, ones, idesc_l, (i > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(barPV);
-          umma_commit(&emptyV[s]);
+          umma_commit(&barPV[b]);
+          umma_commit(&emptyV[b]);
         }
       }
       // No MMA may still be running when TMEM is freed, also after an abort (bounded wait).
@@ -372,7 +395,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       (void)g4a::mbar_wait_bounded(my_end, 0, p.err, G4A_DEVERR_WAIT_MMA);
     }
   } else if (warp >= 4 && warp < 12) {
-    // ------------------------------------------------------------------ Q load, softmax, epilogue
+    // ------------------------------------------------------------------ softmax, epilogue
     const int quarter = warp & 3;                               // TMEM lane quarter of this warp
     const int half = (warp - 4) >> 2;                           // keys [32*half, 32*half + 32) of a block
     const int r = quarter * 32 + lane;                          // tile row = TMEM lane
@@ -381,44 +404,22 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int head = kvh * kHeadsPerKv + (r % kHeadsPerKv);
     const uint32_t hi = p.start_pos + (uint32_t)tok + 1u;
     const uint32_t lo = (p.window != 0u && hi > p.window) ? hi - p.window : 0u;
-    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);   // [half][row]
-    // Q row (half of its dims) into TMEM as f16 pairs: column COL_Q + c holds dims 2c, 2c+1.
-    {
-      const bool valid = tok < p.T;
-      const uint4* src = reinterpret_cast<const uint4*>(p.q16 + ((size_t)tok * p.nqh + head) * HD + half * (HD / 2));
-#pragma unroll
-      for (int c = 0; c < HD / 128; c++) {  // this half's HD/2 dims: 32 columns (64 dims) per store
-        uint32_t w[32];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const uint4 v = valid ? __ldg(src + c * 8 + u) : make_uint4(0u, 0u, 0u, 0u);
-          w[4 * u] = v.x;
-          w[4 * u + 1] = v.y;
-          w[4 * u + 2] = v.z;
-          w[4 * u + 3] = v.w;
-        }
-        tmem_st32(tmem + lane_addr + C::COL_Q + (uint32_t)(half * (HD / 4) + c * 32), w);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(barQ);
-    }
-    const float c2 = p.scale_log2;
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);     // [half][row]
     float* alpha_buf = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
     int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
+    const float c2 = p.scale_log2;
     float m = -INFINITY;
     bool ok = true;
     for (int j = 0; j < nb; j++) {
-      // Waits are made warp-uniform: the tcgen05.ld/st below are warp-collective.
-      ok = __all_sync(0xffffffffu, wait_or_abort(barS, (uint32_t)j & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA));
+      const int b = j & 1;
+      ok = warp_wait(&barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       tc_fence_after();
       uint32_t sv[32];
-      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(32 * half), sv);
+      tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys + 32 * half), sv);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(barSfree);  // the S buffer may be overwritten now
+      if (lane == 0) g4a::mbar_arrive(&barSfree[b]);  // S[b] may be overwritten now
       const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys + 32u * half;
       // Interior blocks (every key visible to every row of the warp) skip the mask.
       const bool interior = __all_sync(0xffffffffu, key0 >= lo && key0 + 32u <= hi) && c2 > 0.f;
@@ -454,15 +455,20 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx : m;
       if (half == 0) {  // publish the row's factor for the correction warps (both halves agree)
+        // slot b was read by the correction of block j-2
+        if (j >= 2) {
+          ok = warp_wait(&barCorr[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
+          if (!ok) break;
+        }
         const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
         const bool need = __any_sync(0xffffffffu, grow && m != -INFINITY);
-        alpha_buf[(j & 1) * kRows + r] = alpha;
-        if (lane == 0) flag_buf[(j & 1) * 4 + quarter] = need ? 1 : 0;
+        alpha_buf[b * kRows + r] = alpha;
+        if (lane == 0) flag_buf[b * 4 + quarter] = need ? 1 : 0;
         __syncwarp();
-        if (lane == 0) g4a::mbar_arrive(&barAlpha[j & 1]);
+        if (lane == 0) g4a::mbar_arrive(&barAlpha[b]);
       }
       m = m_new;
-      // P = 2^(x - m) rounded to f16 pairs (computed before waiting for the previous PV)
+      // P = 2^(x - m) rounded to f16 pairs
       uint32_t pw[16];
       if (m == -INFINITY) {  // no visible key yet in this row
 #pragma unroll
@@ -472,36 +478,33 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 #pragma unroll
         for (int e = 0; e < 16; e++) {
           const float a = g4a::fast_exp2(fmaf(x[2 * e], c2, nm));
-          const float b = g4a::fast_exp2(fmaf(x[2 * e + 1], c2, nm));
-          const __half2 h = __floats2half2_rn(a, b);
+          const float bb = g4a::fast_exp2(fmaf(x[2 * e + 1], c2, nm));
+          const __half2 h = __floats2half2_rn(a, bb);
           pw[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
       } else {
 #pragma unroll
         for (int e = 0; e < 16; e++) {
           const float a = g4a::fast_exp2(x[2 * e] - m);
-          const float b = g4a::fast_exp2(x[2 * e + 1] - m);
-          const __half2 h = __floats2half2_rn(a, b);
+          const float bb = g4a::fast_exp2(x[2 * e + 1] - m);
+          const __half2 h = __floats2half2_rn(a, bb);
           pw[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
       }
-      // single P buffer: PV_{j-1} must have read P_{j-1}
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu,
-                        wait_or_abort(barPV, (uint32_t)(j - 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA));
+      // P[b] was read by PV_{j-2}
+      if (j >= 2) {
+        ok = warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
         if (!ok) break;
         tc_fence_after();
       }
-      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(16 * half), pw);
+      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(b * (kKeys / 2) + 16 * half), pw);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(barP);
+      if (lane == 0) g4a::mbar_arrive(&barP[b]);
     }
     // epilogue: O / l, each half of the row's threads stores half of the columns
-    if (ok)
-      ok = __all_sync(0xffffffffu, wait_or_abort(barPV, (uint32_t)(nb - 1) & 1u, abort_flag, p.err,
-                                                 G4A_DEVERR_WAIT_MMA));
+    if (ok) ok = warp_wait(&barPV[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag, p.err);
     tc_fence_after();
     uint32_t lv[32];
     tmem_ld32(tmem + lane_addr + C::COL_L, lv);
@@ -529,45 +532,45 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const float* alpha_buf = reinterpret_cast<const float*>(smem + C::OFF_ALPHA);
     const volatile int* flag_buf = reinterpret_cast<const volatile int*>(smem + C::OFF_FLAG);
     for (int j = 0; j < nb; j++) {
-      if (!__all_sync(0xffffffffu, wait_or_abort(&barAlpha[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err,
-                                                  G4A_DEVERR_WAIT_MMA)))
-        break;
+      const int b = j & 1;
+      if (!warp_wait(&barAlpha[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err)) break;
       // (block 0: the flag is clear, nothing has been accumulated yet)
-      const float alpha = alpha_buf[(j & 1) * kRows + r];
-      const bool need = flag_buf[(j & 1) * 4 + quarter] != 0;
+      const float alpha = alpha_buf[b * kRows + r];
+      const bool need = flag_buf[b * 4 + quarter] != 0;
       if (need) {
         // O and l hold PV_0 .. PV_{j-1}: wait for the last of them
-        if (!__all_sync(0xffffffffu, wait_or_abort(barPV, (uint32_t)(j - 1) & 1u, abort_flag, p.err,
-                                                   G4A_DEVERR_WAIT_MMA)))
-          break;
+        if (!warp_wait(&barPV[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag, p.err)) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c <= HD / 32; c++) {
-          const uint32_t col = (c < HD / 32) ? (uint32_t)(C::COL_O + c * 32) : C::COL_L;
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_addr + col, o);
+        for (int c = 0; c < HD / 32; c += 2) {  // two 32-column chunks in flight
+          uint32_t o0[32], o1[32];
+          tmem_ld32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32), o0);
+          tmem_ld32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32 + 32), o1);
 #pragma unroll
-          for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          if (c < HD / 32) {
-            tmem_st32(tmem + lane_addr + col, o);
-          } else {
-            uint32_t o16[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) o16[i] = o[i];
-            tmem_st16(tmem + lane_addr + col, o16);
+          for (int i = 0; i < 32; i++) {
+            o0[i] = __float_as_uint(__uint_as_float(o0[i]) * alpha);
+            o1[i] = __float_as_uint(__uint_as_float(o1[i]) * alpha);
           }
+          tmem_st32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32), o0);
+          tmem_st32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32 + 32), o1);
+        }
+        {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_addr + C::COL_L, o);
+          uint32_t o16[16];
+#pragma unroll
+          for (int i = 0; i < 16; i++) o16[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(tmem + lane_addr + C::COL_L, o16);
         }
         tmem_wait_st();
       }
       // A warp with nothing to do could otherwise run two blocks ahead of a slower one and count
       // its arrival into the slower one's phase: arrive only after the previous phase of this
       // parity (block j-2) has completed.
-      if (j >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&barCorr[j & 1], (uint32_t)((j >> 1) - 1) & 1u, abort_flag,
-                                                            p.err, G4A_DEVERR_WAIT_MMA)))
-        break;
+      if (j >= 2 && !warp_wait(&barCorr[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err)) break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(&barCorr[j & 1]);
+      if (lane == 0) g4a::mbar_arrive(&barCorr[b]);
     }
   }
   tc_fence_before();
@@ -621,12 +624,12 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
     if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(prefill_attn_kernel)");
     if (ctx->device < 64) configured[ctx->device] = true;
   }
-  CUtensorMap mk, mv;
+  CUtensorMap mq, mk, mv;
+  if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, "q16")) return s;
   const uint64_t rows = (uint64_t)start_pos + T;
   if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, "the K cache")) return s;
   if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, "the V cache")) return s;
   PrefillParams p = {};
-  p.q16 = q16;
   p.out = out;
   p.T = (int)T;
   p.start_pos = start_pos;
@@ -638,7 +641,7 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   p.err = ctx->dev_err_dev;
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
   cudaError_t e = g4a_launch(prefill_attn_kernel<HD>, dim3((unsigned)(p.ntiles * p.nkh)), dim3(kThreadsP), C::SMEM,
-                             ctx->stream, true, mk, mv, p);
+                             ctx->stream, true, mq, mk, mv, p);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "launch prefill_attn_kernel");
   return G4A_OK;
 }
