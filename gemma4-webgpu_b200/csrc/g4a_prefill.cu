@@ -62,11 +62,11 @@ struct PCfg {
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
   static constexpr int OFF_ONES = OFF_V + kStagesP * KV_BYTES;  // 512 B of f16 ones (l MMA operand)
-  static constexpr int OFF_RED = OFF_ONES + 512;                // [2 halves][128 rows] row maxima
-  static constexpr int OFF_ALPHA = OFF_RED + 2 * kRows * 4;     // [2 parities][128 rows] rescale factors
+  static constexpr int OFF_RED = OFF_ONES + 512;                // [2 parities][2 halves][128 rows] row maxima
+  static constexpr int OFF_ALPHA = OFF_RED + 2 * 2 * kRows * 4; // [2 parities][128 rows] rescale factors
   static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
   static constexpr int OFF_BAR = OFF_FLAG + 64;
-  static constexpr int NBARS = 24;
+  static constexpr int NBARS = 32;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
   // TMEM columns (32-bit each; P holds two f16 per column)
   static constexpr uint32_t COL_O = 0;
@@ -250,6 +250,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* barEnd2 = bars + 18;    // every PV / l MMA done
   uint64_t* barAlpha = bars + 19;   // [2] rescale factors of block j published (4 softmax warps)
   uint64_t* barCorr = bars + 21;    // [2] O/l rescaled for block j (4 correction warps)
+  uint64_t* barXchg = bars + 23;    // [2 parities][4 quarters] row-max halves written (2 softmax warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -275,6 +276,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       g4a::mbar_init(&barPV[s], 1);
       g4a::mbar_init(&barAlpha[s], 4);
       g4a::mbar_init(&barCorr[s], 4);
+      for (int q = 0; q < 4; q++) g4a::mbar_init(&barXchg[s * 4 + q], 2);
     }
     g4a::mbar_init(barQ, 1);
     g4a::mbar_init(barEnd, 1);
@@ -404,7 +406,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int head = kvh * kHeadsPerKv + (r % kHeadsPerKv);
     const uint32_t hi = p.start_pos + (uint32_t)tok + 1u;
     const uint32_t lo = (p.window != 0u && hi > p.window) ? hi - p.window : 0u;
-    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);     // [half][row]
+    float* red = reinterpret_cast<float*>(smem + C::OFF_RED);     // [parity][half][row]
     float* alpha_buf = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
     int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
     const float c2 = p.scale_log2;
@@ -446,11 +448,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         if (interior) mx *= c2;
       }
-      // the row's other half (warp w +- 4, same lanes): exchange through shared memory
-      red[half * kRows + r] = mx;
-      g4a::named_bar_sync(1 + quarter, 64);
-      mx = fmaxf(mx, red[(half ^ 1) * kRows + r]);
-      g4a::named_bar_sync(1 + quarter, 64);  // both read before either writes the next block's max
+      // The row's other half (warp w +- 4, same lanes): exchange through shared memory with a
+      // bounded handshake.  The slots alternate with the block parity; a warp writes slot b again
+      // (block j+2) only after the exchange of block j+1, for which its partner had to arrive
+      // after reading block j's value.
+      red[(b * 2 + half) * kRows + r] = mx;
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(&barXchg[b * 4 + quarter]);
+      ok = warp_wait(&barXchg[b * 4 + quarter], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      if (!ok) break;
+      mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * kRows + r]);
       // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx : m;
@@ -564,10 +571,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         tmem_wait_st();
       }
-      // A warp with nothing to do could otherwise run two blocks ahead of a slower one and count
-      // its arrival into the slower one's phase: arrive only after the previous phase of this
-      // parity (block j-2) has completed.
-      if (j >= 2 && !warp_wait(&barCorr[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err)) break;
+      // barCorr[b] may only complete again (block j) once the PV issuer has consumed its
+      // previous phase (block j-2), or the issuer could find the parity flipped back and wait for
+      // good: wait until PV_{j-2} is done, which the issuer started after that phase.  (Without
+      // this, corrections with nothing to rescale could run two blocks ahead of the issuer.)
+      if (j >= 2 && !warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err)) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) g4a::mbar_arrive(&barCorr[b]);
