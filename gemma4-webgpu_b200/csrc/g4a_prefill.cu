@@ -49,7 +49,7 @@ constexpr int kKeys = 64;                  // keys per block
 constexpr int kStagesP = 2;                // K and V ring depth
 constexpr int kThreadsP = 512;
 constexpr float kLog2eP = 1.4426950408889634f;
-constexpr float kRescaleP = 8.0f;          // lazy rescale threshold (log2 units)
+constexpr float kRescaleP = 15.0f;         // lazy rescale threshold (log2 units): P <= 2^15 stays in f16 range
 
 template <int HD>
 struct PCfg {
