@@ -230,6 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int P = p.B * p.nkh;
+  // Uniform mode (no per-sequence kv_lens): every problem has the same visible key range and
+  // stage count, so the work partition and the position of every stage follow from the launch
+  // parameters alone.  They are computed before the PDL wait, in closed form, and the stages
+  // need no metadata in shared memory.
+  const bool uniform = (p.kv_lens == nullptr);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
@@ -242,19 +247,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   g4a::pdl_launch_dependents();
-  // The work partition below only reads launch parameters and kv_lens.  kv_lens, q and the cache
-  // rows may be written by the preceding kernel: with a programmatic (PDL) launch, wait for it
-  // before reading any of them.
-  g4a::pdl_wait_primary();
 
   // ---- stage range [s0, s1) of this CTA over the flattened stage list (every warp computes it)
   long long S = 0;
-  for (int base = 0; base < P; base += 32) {
-    const int pr = base + lane;
-    int n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
+  int nstg = 0;                // uniform mode: stages per problem
+  uint32_t ulo = 0, uhi = 0;   // uniform mode: visible key range of every problem
+  if (uniform) {
+    key_range(p, 0, ulo, uhi);
+    nstg = uhi > ulo ? (int)((uhi + KPS - 1) / KPS - ulo / KPS) : 0;
+    S = (long long)P * nstg;
+  } else {
+    // kv_lens, like q and the cache rows, may be written by the preceding kernel: with a
+    // programmatic (PDL) launch, wait for it before reading any of them.
+    g4a::pdl_wait_primary();
+    for (int base = 0; base < P; base += 32) {
+      const int pr = base + lane;
+      int n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-    S += n;
+      for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+      S += n;
+    }
   }
   // Only the first min(grid, S) CTAs take part, so every active CTA owns at least one stage and
   // the segment ids blockIdx.x + problem of one problem form a gap-free range.
@@ -264,16 +276,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long s1 = (long long)(blockIdx.x + 1) * S / G;
   const int my_stages = (int)(s1 - s0);
 
-  // =========================== producer role (warp 0 issues the TMA copies)
-  // Stage n of this CTA goes to slot n % kStages.  Warp 0 keeps the cursor (problem, stage
-  // within problem) and, before consuming stage it, issues stage it + kStages - 1 once all
-  // eight warps have released that slot.  A stage is the KPS-aligned block of positions
-  // [key0, key0 + KPS); its valid rows are [kfirst, kend).  Rows outside come from the fill of
-  // out-of-range boxes or from neighbouring cache rows and are masked by the consumers.
-  int prob = 0, j = 0, nprob = 0;
-  uint32_t lo = 0, hi = 0;
-  uint64_t pol = 0;
-  if (warp == 0) {
+  // ---- cursor (problem, stage within the problem) of this CTA's first stage, in every warp
+  int prob0 = 0, j0 = 0;
+  if (uniform) {
+    prob0 = (int)(s0 / nstg);
+    j0 = (int)(s0 - (long long)prob0 * nstg);
+    g4a::pdl_wait_primary();
+  } else {
     long long acc = 0;
     bool found = false;
     for (int base = 0; base < P && !found; base += 32) {
@@ -290,14 +299,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       const unsigned m = __ballot_sync(0xffffffffu, hit);
       if (m) {
         const int src = __ffs(m) - 1;
-        prob = __shfl_sync(0xffffffffu, pr, src);
-        j = (int)(s0 - __shfl_sync(0xffffffffu, lane_start, src));
+        prob0 = __shfl_sync(0xffffffffu, pr, src);
+        j0 = (int)(s0 - __shfl_sync(0xffffffffu, lane_start, src));
         found = true;
       }
       acc += __shfl_sync(0xffffffffu, incl, 31);
     }
-    nprob = stages_of<KPS>(p, prob);
-    key_range(p, prob / p.nkh, lo, hi);
+  }
+
+  // ---- consumer geometry, and the q block (8 heads x HD f32) of the first segment: coalesced
+  // loads issued before the KV stream so that they do not queue behind it, staged through the
+  // merge area of shared memory (rows padded by 8 floats: the fragment reads are conflict-free).
+  const int kg = warp / NDQ;  // key group: keys [16 kg, 16 kg + 16) of every stage
+  const int dq = warp % NDQ;  // output dims [DPW dq, DPW dq + DPW)
+  const int g = lane >> 2;    // head owned by this thread
+  const int c = lane & 3;
+  constexpr int QV = kGroup * HD / 4 / kThreads;  // float4 of the q block per thread
+  constexpr int QROW = HD + 8;                     // staged row stride (floats)
+  static_assert(kGroup * QROW * 4 <= C::NSLOT * C::OSLOT * 4, "q staging fits the merge area");
+  float4 qv[QV];
+  auto load_q = [&](int problem) {
+    const float4* src = reinterpret_cast<const float4*>(p.q + (size_t)problem * kGroup * HD);
+#pragma unroll
+    for (int i = 0; i < QV; i++) qv[i] = src[threadIdx.x + i * kThreads];
+  };
+  // Stores the loaded block, waits for every warp, and builds this thread's A fragments
+  // [q_hi; q_lo] of its KPW k-steps.
+  uint32_t qa[KPW][4];
+  auto stage_q = [&]() {
+#pragma unroll
+    for (int i = 0; i < QV; i++) {
+      const int e = (threadIdx.x + i * kThreads) * 4;
+      *reinterpret_cast<float4*>(oslot + (e / HD) * QROW + (e % HD)) = qv[i];
+    }
+    g4a::named_bar_sync(1, kThreads);
+    const float* qs = oslot + g * QROW + dq * KPW * 16 + 2 * c;
+#pragma unroll
+    for (int ks = 0; ks < KPW; ks++) {
+      const float2 x0 = *reinterpret_cast<const float2*>(qs + ks * 16);
+      const float2 x1 = *reinterpret_cast<const float2*>(qs + ks * 16 + 8);
+      float r0, r1, r2, r3;
+      qa[ks][0] = pack_hi(x0.x, x0.y, r0, r1);
+      qa[ks][1] = pack_f16(r0, r1);
+      qa[ks][2] = pack_hi(x1.x, x1.y, r2, r3);
+      qa[ks][3] = pack_f16(r2, r3);
+    }
+  };
+  load_q(prob0);
+
+  // =========================== producer role (warp 0 issues the TMA copies)
+  // Stage n of this CTA goes to slot n % kStages.  Warp 0 keeps the cursor (problem, stage
+  // within problem) and, before consuming stage it, issues stage it + kStages - 1 once all
+  // eight warps have released that slot.  A stage is the KPS-aligned block of positions
+  // [key0, key0 + KPS); its valid rows are [kfirst, kend).  Rows outside come from the fill of
+  // out-of-range boxes or from neighbouring cache rows and are masked by the consumers.
+  int prob = prob0, j = j0, nprob = 0;
+  uint32_t lo = 0, hi = 0;
+  uint64_t pol = 0;
+  if (warp == 0) {
+    if (uniform) {
+      nprob = nstg;
+      lo = ulo;
+      hi = uhi;
+    } else {
+      nprob = stages_of<KPS>(p, prob);
+      key_range(p, prob / p.nkh, lo, hi);
+    }
     pol = g4a::l2_policy_evict_first();
   }
   auto issue = [&](int n) {
@@ -307,87 +374,134 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     const int seq = prob / p.nkh, kvh = prob % p.nkh;
     const uint32_t key0 = (lo / KPS + (uint32_t)j) * KPS;
-    const int kfirst = (int)(max(lo, key0) - key0);
-    const int kend = (int)(min(hi, key0 + KPS) - key0);
     const uint32_t sK = g4a::smem_u32(stage_base + (size_t)slot * C::STAGE_BYTES);
     const uint32_t sV = sK + NCB * CBB;
-    // Sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller than a stage).
-    const int BR = p.page_table ? min(p.page_size, KPS) : KPS;
-    const int nsub = KPS / BR;
-    // Sub-box s is loaded if it holds a valid row and (paged) its page id is in range.
-    bool need = false;
-    if (lane < nsub) {
-      const int r0 = lane * BR;
-      need = (r0 < kend) && (r0 + BR > kfirst);
-      if (need && p.page_table) {
-        const uint32_t pos = key0 + (uint32_t)r0;
-        const uint32_t pidx = pos / (uint32_t)p.page_size;
-        const int my_page = (pidx < (uint32_t)p.max_pages) ? p.page_table[(size_t)seq * p.max_pages + pidx] : -1;
-        if (my_page < 0 || my_page >= p.num_pages) {
-          if (p.err) atomicExch(p.err, G4A_DEVERR_PAGE);
-          need = false;
+    if (p.page_table == nullptr) {
+      // one op per tensor fills the KPS rows of all HD/64 column boxes
+      if (lane == 0) {
+        if (!uniform) {
+          StageMeta& mt = meta[slot];
+          mt.problem = prob;
+          mt.key0 = (int)key0;
+          mt.kfirst = (int)(max(lo, key0) - key0);
+          mt.kend = (int)(min(hi, key0 + KPS) - key0);
+          int fl = 0;
+          if (n == 0 || j == 0) fl |= F_SEG_FIRST;
+          if (n == my_stages - 1 || j == nprob - 1) fl |= F_SEG_LAST;
+          if (j == 0) fl |= F_PROB_FIRST;
+          if (j == nprob - 1) fl |= F_PROB_LAST;
+          mt.flags = fl;
+          mt.seg = (int)blockIdx.x + prob;
+        }
+        g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)(KPS * 128 * NCB * 2));
+      }
+      __syncwarp();
+      if (lane < 2)
+        tma_load_4d(lane ? sV : sK, lane ? &tmv : &tmk, 0, kvh, (int)key0 - (int)p.row_base, 0, &full[slot], pol);
+    } else {
+      const int kfirst = (int)(max(lo, key0) - key0);
+      const int kend = (int)(min(hi, key0 + KPS) - key0);
+      // Sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller than a stage).
+      const int BR = min(p.page_size, KPS);
+      const int nsub = KPS / BR;
+      // Sub-box s is loaded if it holds a valid row and its page id is in range.
+      bool need = false;
+      if (lane < nsub) {
+        const int r0 = lane * BR;
+        need = (r0 < kend) && (r0 + BR > kfirst);
+        if (need) {
+          const uint32_t pos = key0 + (uint32_t)r0;
+          const uint32_t pidx = pos / (uint32_t)p.page_size;
+          const int my_page =
+              (pidx < (uint32_t)p.max_pages) ? p.page_table[(size_t)seq * p.max_pages + pidx] : -1;
+          if (my_page < 0 || my_page >= p.num_pages) {
+            if (p.err) atomicExch(p.err, G4A_DEVERR_PAGE);
+            need = false;
+          }
         }
       }
-    }
-    const unsigned need_mask = __ballot_sync(0xffffffffu, need);
-    if (lane == 0) {
-      StageMeta& mt = meta[slot];
-      mt.problem = prob;
-      mt.key0 = (int)key0;
-      mt.kfirst = kfirst;
-      mt.kend = kend;
-      int fl = 0;
-      if (n == 0 || j == 0) fl |= F_SEG_FIRST;
-      if (n == my_stages - 1 || j == nprob - 1) fl |= F_SEG_LAST;
-      if (j == 0) fl |= F_PROB_FIRST;
-      if (j == nprob - 1) fl |= F_PROB_LAST;
-      mt.flags = fl;
-      mt.seg = (int)blockIdx.x + prob;
-      g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)__popc(need_mask) * (uint32_t)(BR * 128 * NCB * 2));
-    }
-    __syncwarp();
-    // One op per (sub-box, tensor): each op fills the sub-box rows of all HD/64 column boxes.
-    if (lane < 2 * nsub) {
-      const int s = lane >> 1;
-      const bool is_v = lane & 1;
-      if ((need_mask >> s) & 1u) {
-        const uint32_t dst = (is_v ? sV : sK) + s * NCB * BR * 128;  // sub-box s: [chunk][BR][128 B]
-        const CUtensorMap* map = is_v ? &tmv : &tmk;
-        if (p.page_table) {
+      const unsigned need_mask = __ballot_sync(0xffffffffu, need);
+      if (lane == 0) {
+        if (!uniform) {
+          StageMeta& mt = meta[slot];
+          mt.problem = prob;
+          mt.key0 = (int)key0;
+          mt.kfirst = kfirst;
+          mt.kend = kend;
+          int fl = 0;
+          if (n == 0 || j == 0) fl |= F_SEG_FIRST;
+          if (n == my_stages - 1 || j == nprob - 1) fl |= F_SEG_LAST;
+          if (j == 0) fl |= F_PROB_FIRST;
+          if (j == nprob - 1) fl |= F_PROB_LAST;
+          mt.flags = fl;
+          mt.seg = (int)blockIdx.x + prob;
+        }
+        g4a::mbar_arrive_expect_tx(&full[slot], (uint32_t)__popc(need_mask) * (uint32_t)(BR * 128 * NCB * 2));
+      }
+      __syncwarp();
+      // One op per (sub-box, tensor): each op fills the sub-box rows of all HD/64 column boxes.
+      if (lane < 2 * nsub) {
+        const int s = lane >> 1;
+        const bool is_v = lane & 1;
+        if ((need_mask >> s) & 1u) {
+          const uint32_t dst = (is_v ? sV : sK) + s * NCB * BR * 128;  // sub-box s: [chunk][BR][128 B]
+          const CUtensorMap* map = is_v ? &tmv : &tmk;
           // page id of sub-box s (lane s validated it above; the table line is in L1)
           const uint32_t pos = key0 + (uint32_t)(s * BR);
           const int page = p.page_table[(size_t)seq * p.max_pages + pos / (uint32_t)p.page_size];
           tma_load_5d(dst, map, 0, kvh, (int)(pos % (uint32_t)p.page_size), page, 0, &full[slot], pol);
-        } else {
-          tma_load_4d(dst, map, 0, kvh, (int)key0 - (int)p.row_base, 0, &full[slot], pol);
         }
       }
     }
     if (++j == nprob) {  // advance the cursor to the next problem with stages
       j = 0;
       if (n + 1 < my_stages) {
-        do {
+        if (uniform) {
           prob++;
-          nprob = stages_of<KPS>(p, prob);
-        } while (nprob == 0 && prob < P - 1);
-        key_range(p, prob / p.nkh, lo, hi);
+        } else {
+          do {
+            prob++;
+            nprob = stages_of<KPS>(p, prob);
+          } while (nprob == 0 && prob < P - 1);
+          key_range(p, prob / p.nkh, lo, hi);
+        }
       }
     }
   };
   if (warp == 0) {
-    for (int n = 0; n < kStages - 1 && n < my_stages; n++) issue(n);
+    const int n0 = min(kStages - 1, my_stages);
+    if (uniform && p.page_table == nullptr) {
+      // The first slots are free: lanes 2n and 2n + 1 load K and V of stage n in one go.
+      if (lane < 2 * n0) {
+        const int n = lane >> 1;
+        int pr = prob, jj = j + n;
+        while (jj >= nstg) {
+          jj -= nstg;
+          pr++;
+        }
+        const uint32_t key0 = (lo / KPS + (uint32_t)jj) * KPS;
+        const uint32_t sK = g4a::smem_u32(stage_base + (size_t)n * C::STAGE_BYTES);
+        if ((lane & 1) == 0) g4a::mbar_arrive_expect_tx(&full[n], (uint32_t)(KPS * 128 * NCB * 2));
+        tma_load_4d((lane & 1) ? sK + NCB * CBB : sK, (lane & 1) ? &tmv : &tmk, 0, pr % p.nkh,
+                    (int)key0 - (int)p.row_base, 0, &full[n], pol);
+      }
+      j += n0;
+      while (j >= nprob) {
+        j -= nprob;
+        prob++;
+      }
+    } else {
+      for (int n = 0; n < n0; n++) issue(n);
+    }
   }
+  stage_q();
 
   // =========================== consumer role (all warps)
-  const int kg = warp / NDQ;  // key group: keys [16 kg, 16 kg + 16) of every stage
-  const int dq = warp % NDQ;  // output dims [DPW dq, DPW dq + DPW)
-  const int g = lane >> 2;    // head owned by this thread
-  const int c = lane & 3;
-  uint32_t qa[KPW][4];        // A fragments of [q_hi; q_lo] for this warp's k-steps
   float o[NT][4];             // NT n-tiles of 8 output dims: rows g (hi part) and g+8 (lo part)
   float m_run = -INFINITY;    // running max of head g (base 2)
   float l_part = 0.f;         // this thread's share of the running sum of head g
   bool seg_whole_start = false;
+  int cprob = prob0, cj = j0; // uniform mode: consumer cursor
   // ldmatrix lanes: matrix mi = lane/8, row r8 = lane%8.  A stage tensor is a sequence of
   // sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller), each holding its
   // rows of every 64-dim column chunk as [chunk][BR rows][128 B] with the 128-byte swizzle
@@ -409,20 +523,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && it + kStages - 1 < my_stages) issue(it + kStages - 1);
     const int slot = it % kStages;
     const uint32_t par = (it / kStages) & 1;
+    StageMeta mt;
+    if (uniform) {
+      const uint32_t key0 = (ulo / KPS + (uint32_t)cj) * KPS;
+      mt.problem = cprob;
+      mt.key0 = (int)key0;
+      mt.kfirst = (int)(max(ulo, key0) - key0);
+      mt.kend = (int)(min(uhi, key0 + KPS) - key0);
+      int fl = 0;
+      if (it == 0 || cj == 0) fl |= F_SEG_FIRST;
+      if (it == my_stages - 1 || cj == nstg - 1) fl |= F_SEG_LAST;
+      if (cj == 0) fl |= F_PROB_FIRST;
+      if (cj == nstg - 1) fl |= F_PROB_LAST;
+      mt.flags = fl;
+      mt.seg = (int)blockIdx.x + cprob;
+      if (++cj == nstg) {
+        cj = 0;
+        cprob++;
+      }
+    }
     g4a::mbar_wait_bounded(&full[slot], par, p.err, G4A_DEVERR_WAIT_FULL);
-    const StageMeta mt = meta[slot];
+    if (!uniform) mt = meta[slot];
 
     if (mt.flags & F_SEG_FIRST) {
-      const float* qp = p.q + ((size_t)mt.problem * kGroup + g) * HD + dq * KPW * 16 + 2 * c;
-#pragma unroll
-      for (int ks = 0; ks < KPW; ks++) {
-        const float2 x0 = *reinterpret_cast<const float2*>(qp + ks * 16);
-        const float2 x1 = *reinterpret_cast<const float2*>(qp + ks * 16 + 8);
-        float r0, r1, r2, r3;
-        qa[ks][0] = pack_hi(x0.x, x0.y, r0, r1);
-        qa[ks][1] = pack_f16(r0, r1);
-        qa[ks][2] = pack_hi(x1.x, x1.y, r2, r3);
-        qa[ks][3] = pack_f16(r2, r3);
+      if (it > 0) {  // a later segment: its q block (the merge area is free again)
+        load_q(mt.problem);
+        stage_q();
       }
 #pragma unroll
       for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
@@ -523,7 +649,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) g4a::mbar_arrive(&empty[slot]);
 
     if (mt.flags & F_SEG_LAST) {
-      // ---- merge the NKG key groups of each output slice (tree over shared memory)
+      // ---- merge the NKG key groups of each output slice (tree over shared memory).  The
+      // first barrier orders the q reads of the merge area before the tree's writes.
+      g4a::named_bar_sync(1, kThreads);
       float l_head = l_part;
       l_head += __shfl_xor_sync(0xffffffffu, l_head, 1);
       l_head += __shfl_xor_sync(0xffffffffu, l_head, 2);
@@ -592,91 +720,148 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merge the segments of each problem: one CTA per (problem, head, 16 output dims), 32 segment
-// lanes x 16 dims.  Every thread issues the loads of its (up to 8 per batch) segments before
-// using any of them, so up to 256 segments cost one memory round trip, then merges them with a
-// running log-sum-exp; the 32 lanes combine through shared memory.  mode 0: normalised output
-// rows (problems with a single segment were written by the main kernel); mode 1: one merged
-// partial per problem.
+// Merge the segments of each problem: one CTA per (problem, head, 64 output dims), 512 threads
+// = 32 segment lanes x 16 float4 chunks.  Every thread issues the loads of up to kMergeBatch
+// segments (m, l and a float4 of o) before using any of them, so up to 160 segments cost one
+// memory round trip, and merges them with a log-sum-exp; the two segment lanes of a warp
+// combine by shuffle, the 16 warps through shared memory.  The grid is small (HD/64 x 8 CTAs per
+// problem) and lets its dependents launch at once: the next call's decode CTAs take the SMs it
+// leaves free and warm L2 with their first stages while this merge runs (they read nothing this
+// kernel writes before their own PDL wait).  mode 0: normalised output rows (problems with a
+// single segment were written by the main kernel); mode 1: one merged partial per problem.
+constexpr int kMergeBatch = 5;
+
+// 16-byte store, or four scalar stores when the destination is not 16-byte aligned.
+__device__ __forceinline__ void store_f4(float* dst, float4 v) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    *reinterpret_cast<float4*>(dst) = v;
+  } else {
+    dst[0] = v.x;
+    dst[1] = v.y;
+    dst[2] = v.z;
+    dst[3] = v.w;
+  }
+}
+
 __global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
-  g4a::pdl_wait_primary();
+  g4a::pdl_launch_dependents();
+  // Everything up to the PDL wait depends on launch parameters only.
   const int prob = blockIdx.x, h = blockIdx.y;
   const int hd = p.hd;
-  const int sg = threadIdx.x >> 4, dl = threadIdx.x & 15;
-  const int d = blockIdx.z * 16 + dl;
+  const int ch = threadIdx.x & 15;  // float4 chunk: output dims d .. d + 3
+  const int sl = threadIdx.x >> 4;  // segment lane
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = blockIdx.z * 64 + ch * 4;
   const size_t prow = (size_t)kGroup * (hd + 2);
-  uint32_t lo, hi;
-  key_range(p, prob / p.nkh, lo, hi);
+  float* po = (mode == 0) ? nullptr : part_out + (size_t)prob * prow;
+  float* dst = (mode == 0) ? p.out + ((size_t)prob * kGroup + h) * hd + d : po + 2 * kGroup + (size_t)h * hd + d;
+  const bool single = (p.B * p.nkh == 1);
+  uint32_t lo = 0, hi = 0;
+  int2 r = make_int2(0, 0);
+  if (single) {  // one problem: its segments are the active CTAs 0 .. G-1
+    key_range(p, 0, lo, hi);
+    const uint32_t S = hi > lo ? (hi + p.kps - 1) / p.kps - lo / p.kps : 0;
+    r = make_int2(0, (int)min((uint32_t)p.main_grid, S) - 1);
+  }
+  g4a::pdl_wait_primary();
+  if (!single) key_range(p, prob / p.nkh, lo, hi);  // kv_lens may come from the preceding kernel
   if (hi <= lo) {  // no visible key: zeros (the reference's seq_len 0 output)
-    if (sg == 0) {
-      if (mode == 0) {
-        p.out[((size_t)prob * kGroup + h) * hd + d] = 0.f;
-      } else {
-        float* po = part_out + (size_t)prob * prow;
-        po[2 * kGroup + h * hd + d] = 0.f;
-        if (dl == 0 && blockIdx.z == 0) {
-          po[h] = -INFINITY;
-          po[kGroup + h] = 0.f;
-        }
+    if (sl == 0) {
+      store_f4(dst, make_float4(0.f, 0.f, 0.f, 0.f));
+      if (mode == 1 && ch == 0 && blockIdx.z == 0) {
+        po[h] = -INFINITY;
+        po[kGroup + h] = 0.f;
       }
     }
     return;
   }
-  int2 r;
-  if (p.B * p.nkh == 1) {  // one problem: its segments are the active CTAs 0 .. G-1
-    const uint32_t S = (hi + p.kps - 1) / p.kps - lo / p.kps;
-    r = make_int2(0, (int)min((uint32_t)p.main_grid, S) - 1);
-  } else {
-    r = p.seg_range[prob];
-  }
+  if (!single) r = p.seg_range[prob];
   if (mode == 0 && r.x == r.y) return;  // single segment: the main kernel wrote the row
-  float M = -INFINITY, L = 0.f, acc = 0.f;
-  for (int base = r.x + sg; base <= r.y; base += 32 * 8) {
-    float mv[8], lv[8], ov[8];
+  float M = -INFINITY, L = 0.f;
+  float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int base = r.x + sl; base <= r.y; base += 32 * kMergeBatch) {
+    float mv[kMergeBatch], lv[kMergeBatch];
+    float4 ov[kMergeBatch];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < kMergeBatch; i++) {
       const int s = base + 32 * i;
       const float* row = p.part + (size_t)(s <= r.y ? s : r.x) * prow;
-      mv[i] = row[h];
-      lv[i] = row[kGroup + h];
-      ov[i] = row[2 * kGroup + (size_t)h * hd + d];
+      mv[i] = __ldcg(row + h);
+      lv[i] = __ldcg(row + kGroup + h);
+      ov[i] = __ldcg(reinterpret_cast<const float4*>(row + 2 * kGroup + (size_t)h * hd + d));
       if (s > r.y) mv[i] = -INFINITY;
     }
+    float Mn = M;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      if (mv[i] == -INFINITY) continue;
-      const float Mn = fmaxf(M, mv[i]);
-      const float wa = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
-      const float wb = exp2f(mv[i] - Mn);
-      acc = acc * wa + ov[i] * wb;
-      L = L * wa + lv[i] * wb;
-      M = Mn;
+    for (int i = 0; i < kMergeBatch; i++) Mn = fmaxf(Mn, mv[i]);
+    const float wa = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+    A.x *= wa;
+    A.y *= wa;
+    A.z *= wa;
+    A.w *= wa;
+    L *= wa;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; i++) {
+      const float w = (mv[i] == -INFINITY) ? 0.f : exp2f(mv[i] - Mn);
+      A.x += w * ov[i].x;
+      A.y += w * ov[i].y;
+      A.z += w * ov[i].z;
+      A.w += w * ov[i].w;
+      L += w * lv[i];
     }
+    M = Mn;
   }
-  __shared__ float sM[32][16], sL[32][16], sA[32][16];
-  sM[sg][dl] = M;
-  sL[sg][dl] = L;
-  sA[sg][dl] = acc;
+  // the two segment lanes of this warp (lanes l and l ^ 16 hold the same chunk)
+  {
+    const float Mo = __shfl_xor_sync(0xffffffffu, M, 16);
+    const float Lo = __shfl_xor_sync(0xffffffffu, L, 16);
+    float4 Ao;
+    Ao.x = __shfl_xor_sync(0xffffffffu, A.x, 16);
+    Ao.y = __shfl_xor_sync(0xffffffffu, A.y, 16);
+    Ao.z = __shfl_xor_sync(0xffffffffu, A.z, 16);
+    Ao.w = __shfl_xor_sync(0xffffffffu, A.w, 16);
+    const float Mn = fmaxf(M, Mo);
+    const float wa = (M == -INFINITY) ? 0.f : exp2f(M - Mn);
+    const float wb = (Mo == -INFINITY) ? 0.f : exp2f(Mo - Mn);
+    A.x = A.x * wa + Ao.x * wb;
+    A.y = A.y * wa + Ao.y * wb;
+    A.z = A.z * wa + Ao.z * wb;
+    A.w = A.w * wa + Ao.w * wb;
+    L = L * wa + Lo * wb;
+    M = Mn;
+  }
+  __shared__ float sM[16][16], sL[16][16];
+  __shared__ float4 sA[16][16];
+  if (lane < 16) {
+    sM[warp][lane] = M;
+    sL[warp][lane] = L;
+    sA[warp][lane] = A;
+  }
   __syncthreads();
-  if (sg == 0) {
+  if (threadIdx.x < 16) {
+    const int t = threadIdx.x;
     float Mt = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < 32; i++) Mt = fmaxf(Mt, sM[i][dl]);
-    float Lt = 0.f, At = 0.f;
+    for (int w = 0; w < 16; w++) Mt = fmaxf(Mt, sM[w][t]);
+    float Lt = 0.f;
+    float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < 32; i++) {
-      const float mi = sM[i][dl];
-      if (mi == -INFINITY) continue;
-      const float w = exp2f(mi - Mt);
-      Lt += sL[i][dl] * w;
-      At += sA[i][dl] * w;
+    for (int w = 0; w < 16; w++) {
+      const float mw = sM[w][t];
+      const float wt = (mw == -INFINITY) ? 0.f : exp2f(mw - Mt);
+      const float4 a = sA[w][t];
+      At.x += wt * a.x;
+      At.y += wt * a.y;
+      At.z += wt * a.z;
+      At.w += wt * a.w;
+      Lt += wt * sL[w][t];
     }
     if (mode == 0) {
-      p.out[((size_t)prob * kGroup + h) * hd + d] = At / Lt;
+      const float inv = 1.0f / Lt;
+      store_f4(dst, make_float4(At.x * inv, At.y * inv, At.z * inv, At.w * inv));
     } else {
-      float* po = part_out + (size_t)prob * prow;
-      po[2 * kGroup + h * hd + d] = At;
-      if (dl == 0 && blockIdx.z == 0) {
+      store_f4(dst, At);
+      if (t == 0 && blockIdx.z == 0) {
         po[h] = Mt;
         po[kGroup + h] = Lt;
       }
@@ -913,7 +1098,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   const bool need_merge = (mode == 1) || grid > 1 || stages_upper == 0 || P > 1;
   if (need_merge) {
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_MERGE);
-    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 16), dim3(512), 0, ctx->stream,
+    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 64), dim3(512), 0, ctx->stream,
                                stages_upper > 0, p, mode, part_out);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch merge_segments_kernel");
   }
