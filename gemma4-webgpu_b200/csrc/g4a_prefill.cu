@@ -11,7 +11,7 @@
 // so every row of a tile reads the same K/V rows.  One CTA per tile, heaviest (latest) tiles
 // first.  Q (one TMA load) and 2-stage rings of K and V blocks (64 keys per block, one TMA op
 // per tensor per block, 128-byte swizzle) live in shared memory.  TMEM (HD 256): O [0, 256),
-// l [256, 272), two score buffers S0/S1 [288, 416), two P buffers (f16 pairs) [416, 480).
+// two score buffers S0/S1 [256, 384), two P buffers (f16 pairs) [384, 448).
 // Double-buffering S and P lets the score MMA of block j+1 and the softmax of block j overlap
 // the PV MMA of block j-1, and keeps the softmax off the O-correction chain.
 // Warp roles (512 threads):
@@ -19,18 +19,18 @@
 //   warp 2 lane 0   TMA: V blocks (a V stage is released when PV_j is done).
 //   warp 1          allocates TMEM; lane 0 issues S_j = Q K_j^T (M 128, N 64, K = HD, f16 in /
 //                   f32 accumulate, both operands from shared memory) into S[j % 2].
-//   warp 3 lane 0   issues O += P_j V_j (N = HD) and l += P_j x ones (N = 16), A = P[j % 2] from
-//                   TMEM.
+//   warp 3 lane 0   issues O += P_j V_j (N = HD), A = P[j % 2] from TMEM.
 //   warps 4-11      softmax, two threads per query row (TMEM lane = row; warps w and w+4 take
 //                   keys 0-31 and 32-63 of a block and exchange row maxima through shared
 //                   memory): scores from TMEM (handed back right after the load), window/causal
 //                   mask (boundary blocks only), online softmax in base 2 with lazy rescaling
-//                   (the running max is only raised when a row's max grows by more than 2^8),
-//                   P rounded to f16 into TMEM.  l is accumulated by the tensor core from the
-//                   same f16 P as the output, so numerator and denominator use identical
-//                   weights.  Epilogue: O / l from TMEM to the f32 output.
-//   warps 12-15     correction: when a row's running max was raised, scale its O and l in TMEM
-//                   by 2^(m_old - m_new) after PV_{j-1} and before PV_j.
+//                   (the running max is only raised when a row's max grows by more than 2^15,
+//                   so P <= 2^15 stays in f16 range), P rounded to f16 into TMEM.  Each thread
+//                   sums the same f16-rounded P values in f32 for l (rescaled in registers when
+//                   the max is raised), so numerator and denominator use identical weights.
+//                   Epilogue: the two halves add their l, then O / l from TMEM to the f32 output.
+//   warps 12-15     correction: when a row's running max was raised, scale its O in TMEM by
+//                   2^(m_old - m_new) after PV_{j-1} and before PV_j.
 // Every mbarrier wait is bounded; after a timeout the CTA records an error, stops waiting and
 // frees its TMEM.  Barriers that complete once per block come in pairs (one per block parity)
 // wherever a consumer could otherwise fall two phases behind its producer.
@@ -61,17 +61,16 @@ struct PCfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
-  static constexpr int OFF_ONES = OFF_V + kStagesP * KV_BYTES;  // 512 B of f16 ones (l MMA operand)
-  static constexpr int OFF_RED = OFF_ONES + 512;                // [2 parities][2 halves][128 rows] row maxima
+  static constexpr int OFF_LSUM = OFF_V + kStagesP * KV_BYTES;  // [2 halves][128 rows] row sums (epilogue)
+  static constexpr int OFF_RED = OFF_LSUM + 2 * kRows * 4;      // [2 parities][2 halves][128 rows] row maxima
   static constexpr int OFF_ALPHA = OFF_RED + 2 * 2 * kRows * 4; // [2 parities][128 rows] rescale factors
   static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
   static constexpr int OFF_BAR = OFF_FLAG + 64;
-  static constexpr int NBARS = 32;
+  static constexpr int NBARS = 40;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
   // TMEM columns (32-bit each; P holds two f16 per column)
   static constexpr uint32_t COL_O = 0;
-  static constexpr uint32_t COL_L = HD;
-  static constexpr uint32_t COL_S = HD + 32;                     // S[b] at COL_S + 64 b
+  static constexpr uint32_t COL_S = HD;                          // S[b] at COL_S + 64 b
   static constexpr uint32_t COL_P = COL_S + 2 * kKeys;           // P[b] at COL_P + 32 b
   static constexpr uint32_t TMEM_COLS = (COL_P + kKeys) <= 256 ? 256u : 512u;
   static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte aligned operands");
@@ -99,16 +98,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Descriptor of a K-major operand without swizzle: 8-row x 16-byte core matrices, the next 16
-// bytes of K `lbo_bytes` away, the next 8 rows `sbo_bytes` away.
-__device__ __forceinline__ uint64_t noswz_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;
   return d;
 }
 
@@ -245,12 +234,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* barS = bars + 9;        // [2] S_j in S[j % 2] (tcgen05.commit)
   uint64_t* barSfree = bars + 11;   // [2] S_j loaded by the softmax warps (8 warps)
   uint64_t* barP = bars + 13;       // [2] P_j in P[j % 2] (8 softmax warps)
-  uint64_t* barPV = bars + 15;      // [2] PV_j and l_j done (tcgen05.commit)
+  uint64_t* barPV = bars + 15;      // [2] PV_j done (tcgen05.commit)
   uint64_t* barEnd = bars + 17;     // every score MMA done
-  uint64_t* barEnd2 = bars + 18;    // every PV / l MMA done
+  uint64_t* barEnd2 = bars + 18;    // every PV MMA done
   uint64_t* barAlpha = bars + 19;   // [2] rescale factors of block j published (4 softmax warps)
-  uint64_t* barCorr = bars + 21;    // [2] O/l rescaled for block j (4 correction warps)
+  uint64_t* barCorr = bars + 21;    // [2] O rescaled for block j (4 correction warps)
   uint64_t* barXchg = bars + 23;    // [2 parities][4 quarters] row-max halves written (2 softmax warps)
+  uint64_t* barLsum = bars + 31;    // [4 quarters] row-sum halves written (2 softmax warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -278,6 +268,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       g4a::mbar_init(&barCorr[s], 4);
       for (int q = 0; q < 4; q++) g4a::mbar_init(&barXchg[s * 4 + q], 2);
     }
+    for (int q = 0; q < 4; q++) g4a::mbar_init(&barLsum[q], 2);
     g4a::mbar_init(barQ, 1);
     g4a::mbar_init(barEnd, 1);
     g4a::mbar_init(barEnd2, 1);
@@ -286,9 +277,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
-  }
-  if (threadIdx.x < 128) {  // the all-ones operand of the l MMA (16 rows x 16 keys, no swizzle)
-    reinterpret_cast<uint32_t*>(smem + C::OFF_ONES)[threadIdx.x] = 0x3C003C00u;
   }
   g4a::fence_proxy_async_smem();
   if (warp == 1) {  // TMEM: one CTA per SM (shared memory), so the allocation never waits
@@ -338,7 +326,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------ MMA issuers
     // Two issuing threads, so that the waits of one never leave the tensor pipe without work:
-    // warp 1 issues the score MMAs, warp 3 the PV and l MMAs.  Each commit tracks the MMAs of its
+    // warp 1 issues the score MMAs, warp 3 the PV MMAs.  Each commit tracks the MMAs of its
     // own thread.  Base descriptors are built once; a K step only adds a constant to the
     // start-address field (bits 0-13, in 16-byte units; every operand lies below 256 KB).
     if (lane == 0) {
@@ -369,15 +357,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
       } else {
         constexpr uint32_t idesc_pv = f16_idesc(HD, true);
-        constexpr uint32_t idesc_l = f16_idesc(16, false);
-        const uint64_t ones = noswz_desc(sbase + C::OFF_ONES, 128, 256);
         // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK apart
         // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
         const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
         for (int i = 0; i < nb; i++) {
           const int b = i & 1;
           if (!wait_or_abort(&fullV[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
-          // O and l rescaled for block i (after PV_{i-1}, which the correction warps waited for)
+          // O rescaled for block i (after PV_{i-1}, which the correction warps waited for)
           if (!wait_or_abort(&barCorr[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
           if (!wait_or_abort(&barP[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_MMA)) break;
           tc_fence_after();
@@ -386,7 +372,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           for (int kk = 0; kk < kKeys / 16; kk++) {
             const uint32_t a = tmem + C::COL_P + (uint32_t)(b * (kKeys / 2) + kk * 8);  // 16 keys = 8 columns
             umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-            umma_f16_ts(tmem + C::COL_L, a, ones, idesc_l, (i > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&barPV[b]);
           umma_commit(&emptyV[b]);
@@ -411,6 +396,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
     const float c2 = p.scale_log2;
     float m = -INFINITY;
+    float lsum = 0.f;  // this half's share of the row sum, relative to m
     bool ok = true;
     for (int j = 0; j < nb; j++) {
       const int b = j & 1;
@@ -461,13 +447,14 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx : m;
+      const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
+      lsum *= alpha;
       if (half == 0) {  // publish the row's factor for the correction warps (both halves agree)
         // slot b was read by the correction of block j-2
         if (j >= 2) {
           ok = warp_wait(&barCorr[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
           if (!ok) break;
         }
-        const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
         const bool need = __any_sync(0xffffffffu, grow && m != -INFINITY);
         alpha_buf[b * kRows + r] = alpha;
         if (lane == 0) flag_buf[b * 4 + quarter] = need ? 1 : 0;
@@ -498,6 +485,15 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           pw[e] = *reinterpret_cast<const uint32_t*>(&h);
         }
       }
+      {  // l: the f16-rounded weights, summed in f32
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pw[e]));
+          s4[e & 3] += f.x + f.y;
+        }
+        lsum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      }
       // P[b] was read by PV_{j-2}
       if (j >= 2) {
         ok = warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
@@ -510,12 +506,16 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       __syncwarp();
       if (lane == 0) g4a::mbar_arrive(&barP[b]);
     }
-    // epilogue: O / l, each half of the row's threads stores half of the columns
+    // epilogue: l = both halves' sums (added in the same order by both), then O / l, each half
+    // of the row's threads storing half of the columns
+    float* lsum_buf = reinterpret_cast<float*>(smem + C::OFF_LSUM);  // [half][row]
+    lsum_buf[half * kRows + r] = lsum;
+    __syncwarp();
+    if (lane == 0) g4a::mbar_arrive(&barLsum[quarter]);
+    if (ok) ok = warp_wait(&barLsum[quarter], 0u, abort_flag, p.err);
+    const float l = ok ? lsum_buf[r] + lsum_buf[kRows + r] : 0.f;
     if (ok) ok = warp_wait(&barPV[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag, p.err);
     tc_fence_after();
-    uint32_t lv[32];
-    tmem_ld32(tmem + lane_addr + C::COL_L, lv);
-    const float l = __uint_as_float(lv[0]);
     const bool store = ok && tok < p.T;
     const float inv = (l > 0.f) ? 1.0f / l : 0.f;
     float* orow = p.out + ((size_t)tok * p.nqh + head) * HD + half * (HD / 2);
@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       }
     }
   } else if (warp >= 12) {
-    // ------------------------------------------------------------------ O/l correction
+    // ------------------------------------------------------------------ O correction
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
@@ -545,7 +545,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const float alpha = alpha_buf[b * kRows + r];
       const bool need = flag_buf[b * 4 + quarter] != 0;
       if (need) {
-        // O and l hold PV_0 .. PV_{j-1}: wait for the last of them
+        // O holds PV_0 .. PV_{j-1}: wait for the last of them
         if (!warp_wait(&barPV[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag, p.err)) break;
         tc_fence_after();
 #pragma unroll 1
@@ -560,14 +560,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           }
           tmem_st32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32), o0);
           tmem_st32(tmem + lane_addr + (uint32_t)(C::COL_O + c * 32 + 32), o1);
-        }
-        {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_addr + C::COL_L, o);
-          uint32_t o16[16];
-#pragma unroll
-          for (int i = 0; i < 16; i++) o16[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(tmem + lane_addr + C::COL_L, o16);
         }
         tmem_wait_st();
       }
