@@ -25,7 +25,11 @@
 //                   memory): scores from TMEM (handed back right after the load), window/causal
 //                   mask (boundary blocks only), online softmax in base 2 with lazy rescaling
 //                   (the running max is only raised when a row's max grows by more than 2^15,
-//                   so P <= 2^15 stays in f16 range), P rounded to f16 into TMEM.  Each thread
+//                   so P <= 2^15 stays in f16 range, and then to 2^8 above the new block max,
+//                   which makes the next raise -- an O correction for the whole warp -- rarer:
+//                   Gemma's unit-RMS q and k with scale 1 give scores with a spread of ~16, and
+//                   at 2^0 headroom most 32-row warps needed a correction on most blocks),
+//                   P rounded to f16 into TMEM.  Each thread
 //                   sums the same f16-rounded P values in f32 for l (rescaled in registers when
 //                   the max is raised), so numerator and denominator use identical weights.
 //                   Epilogue: the two halves add their l, then O / l from TMEM to the f32 output.
@@ -50,6 +54,7 @@ constexpr int kStagesP = 2;                // K and V ring depth
 constexpr int kThreadsP = 512;
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 15.0f;         // lazy rescale threshold (log2 units): P <= 2^15 stays in f16 range
+constexpr float kHeadroomP = 8.0f;         // a raised running max is set this far above the block max
 
 template <int HD>
 struct PCfg {
@@ -446,7 +451,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * kRows + r]);
       // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
-      const float m_new = grow ? mx : m;
+      const float m_new = grow ? mx + kHeadroomP : m;
       const float alpha = grow ? ((m == -INFINITY) ? 0.f : g4a::fast_exp2(m - m_new)) : 1.f;
       lsum *= alpha;
       if (half == 0) {  // publish the row's factor for the correction warps (both halves agree)
