@@ -175,6 +175,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Tiled TMA store of a shared-memory box to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void tma_load_4d_p(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
                                               uint64_t* bar, uint64_t pol) {
   asm volatile(
@@ -225,7 +232,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 template <int HD>
 __global__ void __launch_bounds__(kThreadsP, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                        const __grid_constant__ CUtensorMap tmv, const PrefillParams p) {
+                        const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
+                        const PrefillParams p) {
   using C = PCfg<HD>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
@@ -282,6 +290,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmo)) : "memory");
   }
   g4a::fence_proxy_async_smem();
   if (warp == 1) {  // TMEM: one CTA per SM (shared memory), so the allocation never waits
@@ -393,7 +402,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const int r = quarter * 32 + lane;                          // tile row = TMEM lane
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int tok = t0 + r / kHeadsPerKv;
-    const int head = kvh * kHeadsPerKv + (r % kHeadsPerKv);
     const uint32_t hi = p.start_pos + (uint32_t)tok + 1u;
     const uint32_t lo = (p.window != 0u && hi > p.window) ? hi - p.window : 0u;
     float* red = reinterpret_cast<float*>(smem + C::OFF_RED);     // [parity][half][row]
@@ -521,20 +529,39 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const float l = ok ? lsum_buf[r] + lsum_buf[kRows + r] : 0.f;
     if (ok) ok = warp_wait(&barPV[(nb - 1) & 1], (uint32_t)((nb - 1) >> 1) & 1u, abort_flag, p.err);
     tc_fence_after();
-    const bool store = ok && tok < p.T;
+    // O / l is staged in shared memory (the K and V rings are idle now: every MMA is done) as
+    // HD/32 column boxes of [128 rows x 128 B] with the 128-byte swizzle (16-byte chunk q of row
+    // r at q ^ (r & 7), so the 32 rows a warp writes spread over the banks), then written by
+    // HD/32 TMA stores: the tile's rows are 16 tokens x 8 consecutive heads, a box of the
+    // [T, nqh, HD] output, and rows past T are clipped.  (Per-thread stores of 32 different
+    // rows per instruction took ~6 us per tile.)
     const float inv = (l > 0.f) ? 1.0f / l : 0.f;
-    float* orow = p.out + ((size_t)tok * p.nqh + head) * HD + half * (HD / 2);
+    const uint32_t obox = sbase + C::OFF_K;  // HD/32 boxes of 16 KB
+    g4a::fence_proxy_async_smem();  // after the async-proxy use of the rings
+    static_assert(kRows * HD * 4 <= 2 * kStagesP * C::KV_BYTES, "the O tile fits the K and V rings");
 #pragma unroll 1
     for (int c = 0; c < HD / 64; c++) {
+      const int chunk = half * (HD / 64) + c;  // 32-column box
       uint32_t o[32];
-      tmem_ld32(tmem + lane_addr + (uint32_t)(C::COL_O + half * (HD / 2) + c * 32), o);
-      if (store) {
+      tmem_ld32(tmem + lane_addr + (uint32_t)(C::COL_O + chunk * 32), o);
+      const uint32_t row = obox + (uint32_t)chunk * (kRows * 128) + (uint32_t)r * 128;
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(orow + c * 32 + i) =
-              make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                          __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+      for (int q = 0; q < 8; q++) {
+        const uint32_t addr = row + (uint32_t)((q ^ (r & 7)) * 16);
+        asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(__uint_as_float(o[4 * q]) * inv),
+                     "f"(__uint_as_float(o[4 * q + 1]) * inv), "f"(__uint_as_float(o[4 * q + 2]) * inv),
+                     "f"(__uint_as_float(o[4 * q + 3]) * inv)
+                     : "memory");
       }
+    }
+    g4a::fence_proxy_async_smem();  // the generic-proxy writes are visible to the TMA store
+    g4a::named_bar_sync(1, 8 * 32);  // every softmax warp reaches this, also after an abort
+    if (warp == 4 && lane == 0 && ok) {
+#pragma unroll 1
+      for (int chunk = 0; chunk < HD / 32; chunk++)
+        tma_store_3d(&tmo, obox + (uint32_t)chunk * (kRows * 128), chunk * 32, kvh * kHeadsPerKv, t0);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written before the CTA retires
     }
   } else if (warp >= 12) {
     // ------------------------------------------------------------------ O correction
@@ -602,6 +629,21 @@ g4a_status get_encoder_p(g4a_ctx* ctx, PFN_cuTensorMapEncodeTiled_v12000* out) {
 // {64, heads, rows, chunks} f16 map with the chunk index outermost (stride 128 B), 128-byte
 // swizzle, box {64, box_heads, box_rows, chunks}: one TMA op lands a tile as `chunks` column
 // boxes of [box_heads * box_rows rows x 128 B].
+// The f32 output [T, nqh, HD] as {HD, nqh, T} with 128-byte swizzle and box {32, 8, 16}: one
+// TMA store writes 32 columns of a tile's 16 tokens x 8 heads; rows past T are not written.
+g4a_status encode_out_map(g4a_ctx* ctx, CUtensorMap* map, float* base, uint32_t hd, uint32_t nqh, uint32_t T) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (g4a_status s = get_encoder_p(ctx, &enc)) return s;
+  cuuint64_t dims[3] = {hd, nqh, T};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * 4, (cuuint64_t)nqh * hd * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)kHeadsPerKv, (cuuint32_t)kTokPerTile};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return g4a_fail(G4A_ECUDA, "cuTensorMapEncodeTiled failed (%d) for the output", (int)r);
+  return G4A_OK;
+}
+
 g4a_status encode_rows_map(g4a_ctx* ctx, CUtensorMap* map, const void* base, uint32_t hd, uint32_t heads,
                            uint64_t rows, uint32_t box_heads, uint32_t box_rows, const char* what) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
@@ -634,6 +676,8 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   const uint64_t rows = (uint64_t)start_pos + T;
   if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, "the K cache")) return s;
   if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, "the V cache")) return s;
+  CUtensorMap mo;
+  if (g4a_status s = encode_out_map(ctx, &mo, out, HD, nqh, T)) return s;
   PrefillParams p = {};
   p.out = out;
   p.T = (int)T;
@@ -646,7 +690,7 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   p.err = ctx->dev_err_dev;
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
   cudaError_t e = g4a_launch(prefill_attn_kernel<HD>, dim3((unsigned)(p.ntiles * p.nkh)), dim3(kThreadsP), C::SMEM,
-                             ctx->stream, true, mq, mk, mv, p);
+                             ctx->stream, true, mq, mk, mv, mo, p);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "launch prefill_attn_kernel");
   return G4A_OK;
 }
