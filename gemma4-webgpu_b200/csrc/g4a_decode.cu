@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
   }
+  __syncwarp();  // warp 0 was diverged by the initialisation above
   __syncthreads();
   g4a::pdl_launch_dependents();
 

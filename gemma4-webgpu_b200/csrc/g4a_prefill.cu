@@ -299,6 +299,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  __syncwarp();  // warp 0 was diverged by the initialisation above
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -561,7 +562,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       for (int chunk = 0; chunk < HD / 32; chunk++)
         tma_store_3d(&tmo, obox + (uint32_t)chunk * (kRows * 128), chunk * 32, kvh * kHeadsPerKv, t0);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // written before the CTA retires
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // shared memory read before exit
     }
   } else if (warp >= 12) {
     // ------------------------------------------------------------------ O correction
@@ -605,6 +606,10 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       if (lane == 0) g4a::mbar_arrive(&barCorr[b]);
     }
   }
+  // The single-lane roles above leave their warps diverged: reconverge every warp before the
+  // CTA barrier, so that it waits for each lane (an aligned barrier reached by part of a warp
+  // is not a barrier for the rest of it).
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
