@@ -201,6 +201,7 @@ g4a_status g4a_destroy(g4a_ctx* ctx) {
   }
   for (auto e : ctx->prof_free) cudaEventDestroy(e);
   if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->seq_lens) cudaFree(ctx->seq_lens);
   if (ctx->sync_event) cudaEventDestroy(ctx->sync_event);
   if (ctx->dev_err_host) cudaFreeHost((void*)ctx->dev_err_host);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

@@ -54,6 +54,7 @@ struct StageMeta {
 
 struct DecodeParams {
   const float* q;         // [P * 8 (fast) | B * nqh, hd] f32
+  const __half* q16;      // the same queries in f16 (prefill through the decode kernels), or null
   const __half* k;        // cache or page pool base
   const __half* v;
   const int* page_table;  // [B, max_pages] or null (contiguous)
@@ -320,9 +321,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(kGroup * QROW * 4 <= C::NSLOT * C::OSLOT * 4, "q staging fits the merge area");
   float4 qv[QV];
   auto load_q = [&](int problem) {
-    const float4* src = reinterpret_cast<const float4*>(p.q + (size_t)problem * kGroup * HD);
+    if (p.q16 != nullptr) {  // f16 queries: 4 per 8-byte load, exact in f32 (the lo half is 0)
+      const uint2* src = reinterpret_cast<const uint2*>(p.q16 + (size_t)problem * kGroup * HD);
 #pragma unroll
-    for (int i = 0; i < QV; i++) qv[i] = src[threadIdx.x + i * kThreads];
+      for (int i = 0; i < QV; i++) {
+        const uint2 u = src[threadIdx.x + i * kThreads];
+        const float2 a = g4a::h2_to_f2(u.x), b = g4a::h2_to_f2(u.y);
+        qv[i] = make_float4(a.x, a.y, b.x, b.y);
+      }
+    } else {
+      const float4* src = reinterpret_cast<const float4*>(p.q + (size_t)problem * kGroup * HD);
+#pragma unroll
+      for (int i = 0; i < QV; i++) qv[i] = src[threadIdx.x + i * kThreads];
+    }
   };
   // Stores the loaded block, waits for every warp, and builds this thread's A fragments
   // [q_hi; q_lo] of its KPW k-steps.
@@ -882,12 +893,12 @@ __global__ void __launch_bounds__(256) decode_generic_kernel(const DecodeParams 
   constexpr int MAXD = 16;  // dims per lane (head_dim <= 512)
   uint32_t lo, hi;
   key_range(p, seq, lo, hi);
-  const float* qh = p.q + ((size_t)seq * p.nqh + h) * p.hd;
+  const size_t qrow = ((size_t)seq * p.nqh + h) * p.hd;
   float qv[MAXD], o[MAXD];
 #pragma unroll
   for (int i = 0; i < MAXD; i++) {
     const int d = lane + 32 * i;
-    qv[i] = d < p.hd ? qh[d] : 0.f;
+    qv[i] = d < p.hd ? (p.q16 ? __half2float(p.q16[qrow + d]) : p.q[qrow + d]) : 0.f;
     o[i] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
@@ -1202,6 +1213,61 @@ g4a_status noalloc_scratch_address(int device, void** out) {
 }
 
 }  // namespace
+
+// Prefill through the decode kernels, for shapes the tensor-core prefill kernel does not cover
+// (head_dim 512 of Gemma's global layers, GQA ratios other than 8): prompt token i is one decode
+// problem over the shared cache with kv_len = start_pos + i + 1 and the window measured from it,
+// which is exactly the row the reference's per-token prefill (src/engine.ts:2460-2479) computes.
+// The queries are read as f16.  Every problem re-reads its keys (from L2 for prompts whose cache
+// fits), so this path is several times slower than the tensor-core kernel.
+namespace {
+__global__ void seq_lens_kernel(int* lens, uint32_t n, uint32_t first) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) lens[i] = (int)(first + i);
+}
+}  // namespace
+
+g4a_status prefill_via_decode(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
+                              uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale,
+                              uint32_t window) {
+  if (T > (uint32_t)0x7fffffff) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: T too large");
+  if (ctx->seq_lens_cap < T) {
+    // Growing must not free memory that queued kernels still read.
+    G4A_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (ctx->seq_lens) cudaFree(ctx->seq_lens);
+    ctx->seq_lens = nullptr;
+    ctx->seq_lens_cap = 0;
+    const size_t cap = std::max<size_t>(T, 4096);
+    cudaError_t e = cudaMalloc((void**)&ctx->seq_lens, cap * sizeof(int));
+    if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaMalloc(prefill sequence lengths)");
+    ctx->seq_lens_cap = cap;
+  }
+  seq_lens_kernel<<<(T + 255) / 256, 256, 0, ctx->stream>>>(ctx->seq_lens, T, start_pos + 1u);
+  if (g4a_status st = g4a_check_launch("seq_lens_kernel")) return st;
+  DecodeParams p = base_params(nullptr, k, v, nqh, nkh, hd, scale, window, out);
+  p.q16 = reinterpret_cast<const __half*>(q16);
+  p.B = (int)T;
+  p.kv_lens = ctx->seq_lens;
+  p.kv_len_scalar = start_pos + T;  // rows of the cache the tensor maps cover
+  p.err = ctx->dev_err_dev;
+  if (fast_path_ok(nqh, nkh, hd)) {
+    // visible keys: sum over L = start_pos + 1 .. start_pos + T of min(W, L)
+    const long long a = (long long)start_pos + 1, b = (long long)start_pos + T;
+    long long keys;
+    if (window == 0u || (long long)window >= b) {
+      keys = (a + b) * (long long)T / 2;
+    } else if ((long long)window < a) {
+      keys = (long long)window * T;
+    } else {
+      keys = (a + window) * ((long long)window - a + 1) / 2 + (long long)window * (b - window);
+    }
+    keys = keys * nkh + (long long)T * nkh * kps_of(hd);
+    return dispatch_fast(ctx, p, keys, 0, nullptr, true);
+  }
+  g4a_prof_scope ps(ctx, G4A_PROF_DECODE_GENERIC);
+  decode_generic_kernel<<<(unsigned)((size_t)T * nqh), 256, 0, ctx->stream>>>(p, 0, nullptr);
+  return g4a_check_launch("decode_generic_kernel");
+}
 
 extern "C" {
 

@@ -45,6 +45,9 @@ struct g4a_ctx {
   // ranges.  Grown on demand by the decode entry points (or once by g4a_reserve_workspace).
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
+  // Per-token kv lengths of a prefill that runs through the decode kernels (grown on demand).
+  int* seq_lens = nullptr;
+  size_t seq_lens_cap = 0;
   // Device-written error word in mapped pinned host memory: kernels whose bounded waits give
   // up (or that skip an invalid page id) store a nonzero code here; g4a_sync reports and
   // clears it.
@@ -76,6 +79,10 @@ g4a_status g4a_fail(g4a_status st, const char* fmt, ...);
 g4a_status g4a_cuda_fail(cudaError_t e, const char* what);
 g4a_status g4a_check_launch(const char* what);
 g4a_status g4a_ensure_workspace(g4a_ctx* ctx, size_t bytes);
+// Prefill through the decode kernels (shapes the tensor-core prefill kernel does not cover).
+g4a_status prefill_via_decode(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
+                              uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale,
+                              uint32_t window);
 
 #define G4A_CHECK_CTX(ctx)                                                           \
   do {                                                                               \

@@ -708,15 +708,19 @@ extern "C" g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const 
                                        uint32_t sliding_window) {
   G4A_CHECK_CTX(ctx);
   if (!q16 || !k_cache || !v_cache || !out) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: null pointer");
-  if (num_kv_heads == 0 || num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads)
-    return g4a_fail(G4A_EUNSUPPORTED, "g4a_prefill_attn: needs num_q_heads = 8 * num_kv_heads (got %u / %u)",
-                    num_q_heads, num_kv_heads);
-  if (head_dim != 128 && head_dim != 256)
-    return g4a_fail(G4A_EUNSUPPORTED, "g4a_prefill_attn: head_dim %u (supported: 128, 256)", head_dim);
+  if (num_q_heads == 0 || num_kv_heads == 0 || num_kv_heads > num_q_heads)
+    return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: bad head counts nqh=%u nkh=%u", num_q_heads, num_kv_heads);
+  if (head_dim == 0 || head_dim > 512 || (head_dim % 8) != 0)
+    return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: head_dim %u must be a multiple of 8 in [8, 512]", head_dim);
   if ((((uintptr_t)q16) | ((uintptr_t)k_cache) | ((uintptr_t)v_cache) | ((uintptr_t)out)) & 15u)
     return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: pointers must be 16-byte aligned");
   if ((uint64_t)start_pos + T > 0xffffffffull) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: start_pos + T overflows");
   if (T == 0) return G4A_OK;
+  // The tensor-core kernel covers GQA 8:1 at head_dim 128 and 256; every other shape (Gemma's
+  // head_dim 512 global layers among them) runs through the decode kernels.
+  if (num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads || (head_dim != 128 && head_dim != 256))
+    return prefill_via_decode(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, head_dim,
+                              scale, sliding_window);
   if (head_dim == 256)
     return launch_prefill<256>(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
                                sliding_window);

@@ -128,14 +128,44 @@ def test_prefill_repeatable(ctx):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-def test_prefill_rejects_unsupported_shapes(ctx):
-    q16 = torch.zeros((4, 8, 512), dtype=torch.float16, device="cuda")
-    kc = torch.zeros((4, 1, 512), dtype=torch.float16, device="cuda")
-    out = torch.zeros((4, 8, 512), device="cuda")
+# Shapes the tensor-core kernel does not cover run through the decode kernels (fast decode path
+# for head_dim 512 with GQA 8:1, the generic kernel otherwise).
+FALLBACK = [
+    (70, 0, 0, 512, 1, 8),      # Gemma global layer: head_dim 512, causal
+    (90, 300, 512, 512, 1, 8),  # head_dim 512, sliding, after a prefix
+    (33, 5, 0, 256, 1, 4),      # GQA 4:1 (generic kernel)
+    (48, 0, 16, 64, 2, 6),      # GQA 3:1, small head_dim, tiny window
+]
+
+
+@pytest.mark.parametrize("T,start_pos,W,hd,nkh,nqh", FALLBACK)
+def test_prefill_other_shapes_match_oracle(ctx, oracle, T, start_pos, W, hd, nkh, nqh):
+    rng = np.random.default_rng(T + hd + nqh)
+    L = start_pos + T
+    q = rng.standard_normal((T, nqh, hd)).astype(np.float32).astype(np.float16)
+    k = rng.standard_normal((L, nkh, hd)).astype(np.float32).astype(np.float16)
+    v = rng.standard_normal((L, nkh, hd)).astype(np.float32).astype(np.float16)
+    q /= np.float16(np.sqrt(hd) / 4)  # keep the scores in a moderate range
+    q16 = dev(q.view(np.uint16)).view(torch.float16)
+    kc = dev(k.view(np.uint16)).view(torch.float16)
+    vc = dev(v.view(np.uint16)).view(torch.float16)
+    out = torch.full((T, nqh, hd), float("nan"), device="cuda")
+    ctx.prefill_attn(q16, kc, vc, out, T=T, start_pos=start_pos, num_q_heads=nqh, num_kv_heads=nkh, head_dim=hd,
+                     sliding_window=W)
+    ctx.sync()
+    ref = oracle.prefill_rows_f64(q.astype(np.float32), k, v, list(range(T)), start_pos=start_pos, num_q_heads=nqh,
+                                  num_kv_heads=nkh, head_dim=hd, sliding_window=W)
+    assert_attention_close(host(out), ref, what=f"T={T} start={start_pos} W={W} hd={hd} nkh={nkh} nqh={nqh}")
+
+
+def test_prefill_rejects_invalid_shapes(ctx):
+    q16 = torch.zeros((4, 8, 520), dtype=torch.float16, device="cuda")
+    kc = torch.zeros((4, 1, 520), dtype=torch.float16, device="cuda")
+    out = torch.zeros((4, 8, 520), device="cuda")
     with pytest.raises(G4AError) as ei:
-        ctx.prefill_attn(q16, kc, kc, out, T=4, start_pos=0, num_q_heads=8, num_kv_heads=1, head_dim=512)
+        ctx.prefill_attn(q16, kc, kc, out, T=4, start_pos=0, num_q_heads=8, num_kv_heads=1, head_dim=520)
     assert "head_dim" in str(ei.value)
     with pytest.raises(G4AError):
-        ctx.prefill_attn(q16, kc, kc, out, T=4, start_pos=0, num_q_heads=4, num_kv_heads=1, head_dim=256)
+        ctx.prefill_attn(q16, kc, kc, out, T=4, start_pos=0, num_q_heads=1, num_kv_heads=2, head_dim=256)
     ctx.prefill_attn(q16, kc, kc, out, T=0, start_pos=0, num_q_heads=8, num_kv_heads=1, head_dim=256)
     ctx.sync()
