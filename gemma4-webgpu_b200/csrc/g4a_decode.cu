@@ -118,10 +118,12 @@ __device__ __forceinline__ const __half* row_ptr(const DecodeParams& p, const __
 // K and of V as HD/64 column boxes of [KPS rows x 128 B] each, written by TMA with the 128-byte
 // swizzle (16-byte chunk c of row r stored at chunk c ^ (r & 7)), so ldmatrix reads of 8 rows
 // hit 8 different bank groups without padding.
-template <int HD>
+// SHORT halves the stage (twice the k-slices per key group): for calls whose stages of the
+// regular shape would not fill the SMs, more and smaller stages start the CTAs sooner.
+template <int HD, bool SHORT = false>
 struct Cfg {
-  static constexpr int NDQ = HD / 128;                 // score k-slices = output-dim slices
-  static constexpr int DPW = 128;                      // output dims per warp
+  static constexpr int NDQ = (SHORT ? 2 : 1) * (HD / 128);  // score k-slices = output-dim slices
+  static constexpr int DPW = HD / NDQ;                 // output dims per warp
   static constexpr int NT = DPW / 8;                   // n-tiles of the p*V MMA per warp
   static constexpr int NKG = kWarps / NDQ;             // key groups of 16 keys
   static constexpr int KPS = 16 * NKG;                 // keys per stage (64 KB of K+V)
@@ -130,7 +132,7 @@ struct Cfg {
   static constexpr int NCB = HD / 64;                  // 64-dim column boxes per row
   static constexpr int CB_BYTES = KPS * 128;           // one column box of a stage
   static constexpr int STAGE_BYTES = 2 * NCB * CB_BYTES;  // K boxes then V boxes
-  static constexpr int STAGES = 3;                     // depth of the shared-memory ring
+  static constexpr int STAGES = 196608 / STAGE_BYTES;  // depth of the shared-memory ring (192 KB)
   static constexpr int OSTRIDE = DPW + 4;              // floats per head row of a merge slot
   static constexpr int OSLOT = kGroup * OSTRIDE + 2 * kGroup;  // o[8][DPW+4] | m[8] | l[8]
   static constexpr int NSLOT = (NKG / 2) * NDQ;
@@ -138,7 +140,7 @@ struct Cfg {
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)NSLOT * OSLOT * 4 +
                                  (size_t)SX_FLOATS * 4 + STAGES * sizeof(StageMeta) + 2 * STAGES * 8 + 64;
   static_assert(NKG >= 2 && NKG * NDQ == kWarps && NT % 2 == 0 && KPW % 4 == 0, "tile shape");
-  static_assert(CB_BYTES % 1024 == 0 && STAGE_BYTES == 65536, "swizzle atoms / stage size");
+  static_assert(CB_BYTES % 1024 == 0 && STAGES >= 3, "swizzle atoms / ring depth");
   static_assert(SMEM <= 232448, "shared memory");
 };
 
@@ -210,11 +212,11 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
 // the p*V MMA, the masking of out-of-range keys (their scores become -inf and their V halves in
 // the B fragments become 0) and the rescaling of its output accumulators are all thread-local;
 // only the row max and the final row sum need two shuffles.
-template <int HD>
+template <int HD, bool SHORT>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_splitkv_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
-  using C = Cfg<HD>;
+  using C = Cfg<HD, SHORT>;
   constexpr int NDQ = C::NDQ, KPS = C::KPS, KPW = C::KPW, NCB = C::NCB, CBB = C::CB_BYTES;
   constexpr int NKG = C::NKG, NT = C::NT, DPW = C::DPW, kStages = C::STAGES;
 
@@ -997,12 +999,12 @@ bool paged_fast_ok(uint32_t page_size, uint32_t hd) {
   return page_size >= 8 && page_size <= 256 * 1024 && (page_size % kps == 0 || kps % page_size == 0);
 }
 
-template <int HD>
+template <int HD, bool SHORT>
 g4a_status configure_kernel(g4a_ctx* ctx) {
   static bool done[64] = {false};
   if (ctx->device < 64 && done[ctx->device]) return G4A_OK;
-  cudaError_t e = cudaFuncSetAttribute(decode_splitkv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)Cfg<HD>::SMEM);
+  cudaError_t e = cudaFuncSetAttribute(decode_splitkv_kernel<HD, SHORT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)Cfg<HD, SHORT>::SMEM);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(decode_splitkv_kernel)");
   if (ctx->device < 64) done[ctx->device] = true;
   return G4A_OK;
@@ -1065,11 +1067,11 @@ struct FixedScratch {
   const char* who;  // entry-point name for error messages
 };
 
-template <int HD>
+template <int HD, bool SHORT>
 g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, int mode, float* part_out, bool pdl,
                        const FixedScratch* fixed) {
-  using C = Cfg<HD>;
-  if (g4a_status s = configure_kernel<HD>(ctx)) return s;
+  using C = Cfg<HD, SHORT>;
+  if (g4a_status s = configure_kernel<HD, SHORT>(ctx)) return s;
   const int P = p.B * p.nkh;
   int grid = (int)std::min<long long>(stages_upper + P, (long long)ctx->num_sms);
   if (grid < 1) grid = 1;
@@ -1102,7 +1104,7 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
     if (g4a_status s = encode_kv_maps(ctx, p, C::KPS, rows, &mk, &mv)) return s;
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_SPLITKV);
     cudaError_t e =
-        g4a_launch(decode_splitkv_kernel<HD>, dim3(grid), dim3(kThreads), C::SMEM, ctx->stream, pdl, p, mk, mv);
+        g4a_launch(decode_splitkv_kernel<HD, SHORT>, dim3(grid), dim3(kThreads), C::SMEM, ctx->stream, pdl, p, mk, mv);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch decode_splitkv_kernel");
   }
   // The merge kernel is needed when a problem can span several CTAs, for zero-length problems,
@@ -1121,12 +1123,24 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
 g4a_status dispatch_fast(g4a_ctx* ctx, DecodeParams& p, long long keys_upper, int mode, float* part_out, bool pdl,
                          const FixedScratch* fixed = nullptr) {
   switch (p.hd) {
-    case 128:
-      return launch_fast<128>(ctx, p, (keys_upper + Cfg<128>::KPS - 1) / Cfg<128>::KPS, mode, part_out, pdl, fixed);
-    case 256:
-      return launch_fast<256>(ctx, p, (keys_upper + Cfg<256>::KPS - 1) / Cfg<256>::KPS, mode, part_out, pdl, fixed);
+    // Calls whose regular stages would leave SMs idle use the half-size stages.
+    case 128: {
+      const long long st = (keys_upper + Cfg<128>::KPS - 1) / Cfg<128>::KPS;
+      if (st < ctx->num_sms)
+        return launch_fast<128, true>(ctx, p, (keys_upper + Cfg<128, true>::KPS - 1) / Cfg<128, true>::KPS, mode,
+                                      part_out, pdl, fixed);
+      return launch_fast<128, false>(ctx, p, st, mode, part_out, pdl, fixed);
+    }
+    case 256: {
+      const long long st = (keys_upper + Cfg<256>::KPS - 1) / Cfg<256>::KPS;
+      if (st < ctx->num_sms)
+        return launch_fast<256, true>(ctx, p, (keys_upper + Cfg<256, true>::KPS - 1) / Cfg<256, true>::KPS, mode,
+                                      part_out, pdl, fixed);
+      return launch_fast<256, false>(ctx, p, st, mode, part_out, pdl, fixed);
+    }
     case 512:
-      return launch_fast<512>(ctx, p, (keys_upper + Cfg<512>::KPS - 1) / Cfg<512>::KPS, mode, part_out, pdl, fixed);
+      return launch_fast<512, false>(ctx, p, (keys_upper + Cfg<512>::KPS - 1) / Cfg<512>::KPS, mode, part_out, pdl,
+                                     fixed);
     default:
       return g4a_fail(G4A_EINVAL, "decode: unsupported head_dim %d", p.hd);
   }
