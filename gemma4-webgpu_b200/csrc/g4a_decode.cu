@@ -9,7 +9,8 @@
 //   - kv head of q head h is h * NKH / NQH (attn_score.wgsl:31); scale multiplies the dot
 //     (attn_score.wgsl:39); output f32 [NQH, HD] (attn_output.wgsl:22); L = 0 gives zeros.
 //
-// Fast path (NQH = 8 * NKH, HD in {128, 256, 512}): persistent CTAs, one per SM, 8 warps.
+// Fast path (NQH = 8 * NKH, HD in {128, 256, 512}): persistent CTAs, one per SM, 8 warps.  A
+// call whose stages would not fill the SMs (short contexts) uses half-size stages instead.
 // The flattened list of "stages" (64 keys for HD 256) of every (sequence, kv head) problem is
 // split evenly over the grid, so a CTA may cover the end of one problem and the start of the
 // next.  Warp 0 is also the producer: it TMA-bulk-copies every K and V row of a stage (no
