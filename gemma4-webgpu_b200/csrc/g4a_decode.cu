@@ -735,11 +735,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merge the segments of each problem: one CTA per (problem, head, 64 output dims), 512 threads
-// = 32 segment lanes x 16 float4 chunks.  Every thread issues the loads of up to kMergeBatch
-// segments (m, l and a float4 of o) before using any of them, so up to 160 segments cost one
+// Merge the segments of each problem: one CTA per (problem, head, 64 output dims), NW warps =
+// 2 NW segment lanes x 16 float4 chunks.  Every thread issues the loads of up to kMergeBatch
+// segments (m, l and a float4 of o) before using any of them, so up to 10 NW segments cost one
 // memory round trip, and merges them with a log-sum-exp; the two segment lanes of a warp
-// combine by shuffle, the 16 warps through shared memory.  The grid is small (HD/64 x 8 CTAs per
+// combine by shuffle, the NW warps through shared memory.  The grid is small (HD/64 x 8 CTAs per
 // problem) and lets its dependents launch at once: the next call's decode CTAs take the SMs it
 // leaves free and warm L2 with their first stages while this merge runs (they read nothing this
 // kernel writes before their own PDL wait).  mode 0: normalised output rows (problems with a
@@ -758,7 +758,10 @@ __device__ __forceinline__ void store_f4(float* dst, float4 v) {
   }
 }
 
-__global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
+// NW warps: 16 for one problem (its segments are every active CTA), 2 for many problems (each
+// split over a few CTAs), so a batch launches small CTAs that all fit in one wave.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) merge_segments_kernel(const DecodeParams p, int mode, float* part_out) {
   g4a::pdl_launch_dependents();
   // Everything up to the PDL wait depends on launch parameters only.
   const int prob = blockIdx.x, h = blockIdx.y;
@@ -794,12 +797,12 @@ __global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams 
   if (mode == 0 && r.x == r.y) return;  // single segment: the main kernel wrote the row
   float M = -INFINITY, L = 0.f;
   float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int base = r.x + sl; base <= r.y; base += 32 * kMergeBatch) {
+  for (int base = r.x + sl; base <= r.y; base += 2 * NW * kMergeBatch) {
     float mv[kMergeBatch], lv[kMergeBatch];
     float4 ov[kMergeBatch];
 #pragma unroll
     for (int i = 0; i < kMergeBatch; i++) {
-      const int s = base + 32 * i;
+      const int s = base + 2 * NW * i;
       const float* row = p.part + (size_t)(s <= r.y ? s : r.x) * prow;
       mv[i] = __ldcg(row + h);
       lv[i] = __ldcg(row + kGroup + h);
@@ -845,8 +848,8 @@ __global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams 
     L = L * wa + Lo * wb;
     M = Mn;
   }
-  __shared__ float sM[16][16], sL[16][16];
-  __shared__ float4 sA[16][16];
+  __shared__ float sM[NW][16], sL[NW][16];
+  __shared__ float4 sA[NW][16];
   if (lane < 16) {
     sM[warp][lane] = M;
     sL[warp][lane] = L;
@@ -857,11 +860,11 @@ __global__ void __launch_bounds__(512) merge_segments_kernel(const DecodeParams 
     const int t = threadIdx.x;
     float Mt = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 16; w++) Mt = fmaxf(Mt, sM[w][t]);
+    for (int w = 0; w < NW; w++) Mt = fmaxf(Mt, sM[w][t]);
     float Lt = 0.f;
     float4 At = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < 16; w++) {
+    for (int w = 0; w < NW; w++) {
       const float mw = sM[w][t];
       const float wt = (mw == -INFINITY) ? 0.f : exp2f(mw - Mt);
       const float4 a = sA[w][t];
@@ -1113,7 +1116,10 @@ g4a_status launch_fast(g4a_ctx* ctx, DecodeParams& p, long long stages_upper, in
   const bool need_merge = (mode == 1) || grid > 1 || stages_upper == 0 || P > 1;
   if (need_merge) {
     g4a_prof_scope ps(ctx, G4A_PROF_DECODE_MERGE);
-    cudaError_t e = g4a_launch(merge_segments_kernel, dim3(P, kGroup, HD / 64), dim3(512), 0, ctx->stream,
+    cudaError_t e = (P == 1)
+                        ? g4a_launch(merge_segments_kernel<16>, dim3(P, kGroup, HD / 64), dim3(512), 0, ctx->stream,
+                                     stages_upper > 0, p, mode, part_out)
+                        : g4a_launch(merge_segments_kernel<2>, dim3(P, kGroup, HD / 64), dim3(64), 0, ctx->stream,
                                stages_upper > 0, p, mode, part_out);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "launch merge_segments_kernel");
   }
