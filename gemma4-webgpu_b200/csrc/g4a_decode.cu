@@ -277,8 +277,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the segment ids blockIdx.x + problem of one problem form a gap-free range.
   const long long G = (long long)gridDim.x < S ? (long long)gridDim.x : S;
   if ((long long)blockIdx.x >= G) return;  // uniform across the CTA
-  const long long s0 = (long long)blockIdx.x * S / G;
-  const long long s1 = (long long)(blockIdx.x + 1) * S / G;
+  // The CTAs with the lowest indices take the one extra stage: the last CTAs of the grid are
+  // the ones that start late (they wait for the SMs the previous kernel still occupies).
+  const long long q_st = S / G, r_st = S % G, b_st = (long long)blockIdx.x;
+  const long long s0 = b_st * q_st + (b_st < r_st ? b_st : r_st);
+  const long long s1 = s0 + q_st + (b_st < r_st ? 1 : 0);
   const int my_stages = (int)(s1 - s0);
 
   // ---- cursor (problem, stage within the problem) of this CTA's first stage, in every warp
