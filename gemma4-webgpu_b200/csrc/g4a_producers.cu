@@ -10,13 +10,16 @@
 // as the WGSL `shared_sum` reduction, and every product/quotient is an explicit IEEE
 // round-to-nearest intrinsic (no contraction), so the results are bit-identical to the CPU
 // restatement.  The RoPE frequency is 1/RN32(theta^(2i/HD)) with the power evaluated in double
-// and rounded once, and cos/sin are the double-precision values of the f32 angle rounded to
-// f32: a fixed definition of the WGSL built-ins whose precision the reference leaves to the
-// WebGPU implementation.
+// and rounded once -- on the host, once per launch, and passed to the kernels as a table
+// (it depends only on theta and HD) -- and cos/sin are the double-precision values of the f32
+// angle rounded to f32: a fixed definition of the WGSL built-ins whose precision the reference
+// leaves to the WebGPU implementation.
 //
 // These kernels move a few KB per token; they are launch-bound, which is why the decode path
 // runs q, k and v through one launch (g4a_attn_decode_layer) and prefill runs all T tokens
 // through one launch (g4a_prefill_qkv_prep).
+#include <math.h>
+
 #include "g4a_internal.cuh"
 
 namespace {
@@ -53,11 +56,23 @@ __device__ __forceinline__ float head_rms(const float* x, int hd, float eps, flo
   return __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
 }
 
+// RN32(theta^(2i/HD)) for the pairs of a head, evaluated on the host (double pow, rounded once).
+struct RopePow {
+  float p[kMaxHeadDim / 2];
+};
+
+RopePow make_rope_pow(float theta, uint32_t hd) {
+  RopePow t;
+  for (uint32_t i = 0; i < hd / 2 && i < (uint32_t)(kMaxHeadDim / 2); i++) {
+    const float e = (float)(i * 2u) / (float)hd;
+    t.p[i] = (float)pow((double)theta, (double)e);
+  }
+  return t;
+}
+
 // RoPE inverse frequency of pair i (fused_per_head_norm_rope.wgsl:50-54).
-__device__ __forceinline__ float rope_freq(int i, int hd, float theta, const __half* rope_freqs, uint32_t apply_div) {
-  float e = __fdiv_rn((float)(i * 2), (float)hd);
-  float p = __double2float_rn(pow((double)theta, (double)e));
-  float freq = __fdiv_rn(1.0f, p);
+__device__ __forceinline__ float rope_freq(int i, const RopePow& tab, const __half* rope_freqs, uint32_t apply_div) {
+  float freq = __fdiv_rn(1.0f, tab.p[i]);
   if (apply_div != 0u) freq = __fdiv_rn(freq, __half2float(rope_freqs[i]));
   return freq;
 }
@@ -65,7 +80,7 @@ __device__ __forceinline__ float rope_freq(int i, int hd, float theta, const __h
 // Normalise one head (x * w / rms) and rotate it.  `in` may alias `out_f32`.  Either output may
 // be null.  xs is hd floats of shared memory, red 256 floats.
 __device__ void norm_rope_head(const float* in, float* out_f32, __half* out_f16, const __half* w,
-                               const __half* rope_freqs, int hd, float eps, uint32_t position, float theta,
+                               const __half* rope_freqs, int hd, float eps, uint32_t position, const RopePow& tab,
                                uint32_t apply_div, float* xs, float* red) {
   for (int i = threadIdx.x; i < hd; i += kWG) xs[i] = in[i];
   __syncthreads();
@@ -75,7 +90,7 @@ __device__ void norm_rope_head(const float* in, float* out_f32, __half* out_f16,
   const int half_dim = hd / 2;
   const float posf = __uint2float_rn(position);
   for (int i = threadIdx.x; i < half_dim; i += kWG) {
-    float freq = rope_freq(i, hd, theta, rope_freqs, apply_div);
+    float freq = rope_freq(i, tab, rope_freqs, apply_div);
     float angle = __fmul_rn(posf, freq);
     double s, c;
     sincos((double)angle, &s, &c);
@@ -111,12 +126,12 @@ __device__ void vnorm_head(const float* in, float* out_f32, __half* out_f16, int
 }
 
 __global__ void __launch_bounds__(kWG) norm_rope_kernel(float* x, const __half* w, const __half* rope_freqs, int hd,
-                                                         float eps, uint32_t position, float theta,
-                                                         uint32_t apply_div) {
+                                                         float eps, uint32_t position,
+                                                         const __grid_constant__ RopePow tab, uint32_t apply_div) {
   __shared__ float xs[kMaxHeadDim];
   __shared__ float red[kWG];
   float* xh = x + (size_t)blockIdx.x * hd;
-  norm_rope_head(xh, xh, nullptr, w, rope_freqs, hd, eps, position, theta, apply_div, xs, red);
+  norm_rope_head(xh, xh, nullptr, w, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
 }
 
 __global__ void __launch_bounds__(kWG) rms_norm_no_weight_kernel(float* x, int hd, float eps) {
@@ -146,18 +161,18 @@ __global__ void __launch_bounds__(kWG) decode_prep_kernel(float* q, float* k, fl
                                                            const __half* kw, const __half* rope_freqs,
                                                            __half* k_cache, __half* v_cache, int nqh, int nkh,
                                                            int hd, float eps, uint32_t position, uint32_t slot,
-                                                           float theta, uint32_t apply_div) {
+                                                           const __grid_constant__ RopePow tab, uint32_t apply_div) {
   __shared__ float xs[kMaxHeadDim];
   __shared__ float red[kWG];
   const int b = blockIdx.x;
   if (b < nqh) {
     float* qh = q + (size_t)b * hd;
-    norm_rope_head(qh, qh, nullptr, qw, rope_freqs, hd, eps, position, theta, apply_div, xs, red);
+    norm_rope_head(qh, qh, nullptr, qw, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
   } else {
     const int j = b - nqh;
     const size_t row = ((size_t)slot * nkh + j) * hd;
     float* kh = k + (size_t)j * hd;
-    norm_rope_head(kh, kh, k_cache + row, kw, rope_freqs, hd, eps, position, theta, apply_div, xs, red);
+    norm_rope_head(kh, kh, k_cache + row, kw, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
     float* vh = v + (size_t)j * hd;
     vnorm_head(vh, vh, v_cache + row, hd, eps, true, xs, red);
   }
@@ -181,7 +196,8 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, cons
                                                              const __half* qw, const __half* kw,
                                                              const __half* rope_freqs, __half* q16, __half* k_cache,
                                                              __half* v_cache, int nqh, int nkh, int hd, float eps,
-                                                             uint32_t start_pos, float theta, uint32_t apply_div) {
+                                                             uint32_t start_pos, const __grid_constant__ RopePow tab,
+                                                             uint32_t apply_div) {
   __shared__ float sn[kPrepMaxHd / 2], cs[kPrepMaxHd / 2];
   const int t = threadIdx.x, lane = t & 31;
   const uint32_t i = blockIdx.x;
@@ -189,7 +205,7 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, cons
   const int half_dim = hd / 2;
   const float posf = __uint2float_rn(pos);
   for (int p = t; p < half_dim; p += blockDim.x) {
-    const float angle = __fmul_rn(posf, rope_freq(p, hd, theta, rope_freqs, apply_div));
+    const float angle = __fmul_rn(posf, rope_freq(p, tab, rope_freqs, apply_div));
     double s_, c_;
     sincos((double)angle, &s_, &c_);
     sn[p] = __double2float_rn(s_);
@@ -270,7 +286,8 @@ g4a_status g4a_norm_rope(g4a_ctx* ctx, float* x, const uint16_t* weight, const u
     return g4a_fail(G4A_EINVAL, "g4a_norm_rope: apply_divisor set but rope_freqs is null");
   g4a_prof_scope ps(ctx, G4A_PROF_NORM_ROPE);
   norm_rope_kernel<<<num_heads, kWG, 0, ctx->stream>>>(x, (const __half*)weight, (const __half*)rope_freqs,
-                                                       (int)head_dim, eps, position, theta, apply_divisor);
+                                                       (int)head_dim, eps, position,
+                                                       make_rope_pow(theta, head_dim), apply_divisor);
   return g4a_check_launch("norm_rope_kernel");
 }
 
@@ -325,7 +342,8 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
   prefill_prep_kernel<<<grid, warps * 32, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
                                                      (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
                                                      (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads,
-                                                     (int)head_dim, eps, start_pos, theta, apply_divisor);
+                                                     (int)head_dim, eps, start_pos,
+                                                     make_rope_pow(theta, head_dim), apply_divisor);
   return g4a_check_launch("prefill_prep_kernel");
 }
 
@@ -344,6 +362,6 @@ g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, float* q, float* k, float* v, co
   decode_prep_kernel<<<blocks, kWG, 0, ctx->stream>>>(q, k, v, (const __half*)qw, (const __half*)kw,
                                                       (const __half*)rope_freqs, (__half*)k_cache,
                                                       (__half*)v_cache, (int)nqh, (int)nkh, (int)hd, eps, position,
-                                                      slot, theta, apply_div);
+                                                      slot, make_rope_pow(theta, hd), apply_div);
   return g4a_check_launch("decode_prep_kernel");
 }
