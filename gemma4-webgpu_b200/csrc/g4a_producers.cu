@@ -182,16 +182,19 @@ __global__ void __launch_bounds__(kWG) decode_prep_kernel(float* q, float* k, fl
 
 // Prefill input stage: one CTA per token (grid T), one warp per head (q heads, then k heads,
 // then v heads).  Token i is at position start_pos + i and is stored at cache row start_pos + i;
-// inputs are left untouched.  The RoPE sin/cos of the position are computed once per token.  A
+// inputs are left untouched.  The RoPE sin/cos of the position are computed once per token, and
+// the two norm weights are widened to f32 once per token, both into shared memory.  A
 // warp reproduces the 256-thread WGSL sum-of-squares tree exactly: lane l holds elements
 // l + 32j, so thread t = l + 32j's partial sum (its elements t, t + 256, ... added from 0 in
 // order) and the first three halving levels (128, 64, 32) are lane-local adds in the same order,
 // and the last five levels are the same shuffles as in wg_tree_sum.  RoPE pairs (p, p + hd/2) are
 // lane-local too.  Every output is bit-identical to the single-head kernels.  head_dim must be
-// a multiple of 64 and at most 512.
+// a multiple of 64 and at most 512; NJ = head_dim / 32 is a template argument, so every index
+// into the lane's elements is a compile-time constant and they stay in registers.
 constexpr int kPrepMaxHd = 512;
 constexpr int kPrepMaxWarps = 32;
 
+template <int NJ>
 __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, const float* k, const float* v,
                                                              const __half* qw, const __half* kw,
                                                              const __half* rope_freqs, __half* q16, __half* k_cache,
@@ -199,6 +202,7 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, cons
                                                              uint32_t start_pos, const __grid_constant__ RopePow tab,
                                                              uint32_t apply_div) {
   __shared__ float sn[kPrepMaxHd / 2], cs[kPrepMaxHd / 2];
+  __shared__ float sw[2][kPrepMaxHd];  // q_norm and k_norm weights as f32
   const int t = threadIdx.x, lane = t & 31;
   const uint32_t i = blockIdx.x;
   const uint32_t pos = start_pos + i;
@@ -211,24 +215,29 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, cons
     sn[p] = __double2float_rn(s_);
     cs[p] = __double2float_rn(c_);
   }
+  for (int p = t; p < hd; p += blockDim.x) {
+    sw[0][p] = __half2float(qw[p]);
+    sw[1][p] = __half2float(kw[p]);
+  }
   __syncthreads();
   const int H = nqh + 2 * nkh;
-  const int nj = hd / 32;  // elements per lane (2..16)
   for (int h = t >> 5; h < H; h += blockDim.x >> 5) {
     const bool is_q = h < nqh, is_k = !is_q && h < nqh + nkh;
     const float* src = is_q ? q + ((size_t)i * nqh + h) * hd
                        : is_k ? k + ((size_t)i * nkh + (h - nqh)) * hd
                               : v + ((size_t)i * nkh + (h - nqh - nkh)) * hd;
-    float x[16];
+    float x[NJ];
 #pragma unroll
-    for (int j = 0; j < 16; j++) x[j] = (j < nj) ? src[lane + 32 * j] : 0.f;
+    for (int j = 0; j < NJ; j++) x[j] = src[lane + 32 * j];
     // thread t = lane + 32j of the WGSL workgroup: partial over elements t, t + 256
     float s8[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      float part = __fmul_rn(x[j], x[j]);  // 0 + x*x
-      if (j + 8 < nj) part = __fadd_rn(part, __fmul_rn(x[j + 8], x[j + 8]));
-      s8[j] = (j < nj) ? part : 0.f;
+      // (j % NJ) keeps every index in range at compile time; the guards select the live terms.
+      float part = 0.f;
+      if (j < NJ) part = __fmul_rn(x[j % NJ], x[j % NJ]);  // 0 + x*x
+      if (j + 8 < NJ) part = __fadd_rn(part, __fmul_rn(x[(j + 8) % NJ], x[(j + 8) % NJ]));
+      s8[j] = part;
     }
 #pragma unroll
     for (int j = 0; j < 4; j++) s8[j] = __fadd_rn(s8[j], s8[j + 4]);  // stride 128
@@ -241,24 +250,21 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(const float* q, cons
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps));
     __half* dst;
     if (is_q || is_k) {
-      const __half* w = is_q ? qw : kw;
+      const float* w = sw[is_q ? 0 : 1];
       dst = is_q ? q16 + ((size_t)i * nqh + h) * hd : k_cache + ((size_t)pos * nkh + (h - nqh)) * hd;
-      const int pj = nj / 2;  // pair partner of element j is j + pj
+      constexpr int pj = NJ / 2;  // pair partner of element j is j + pj
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        if (j < pj) {
-          const int p = lane + 32 * j;
-          const float x0 = __fdiv_rn(__fmul_rn(x[j], __half2float(w[p])), rms);
-          const float x1 = __fdiv_rn(__fmul_rn(x[j + pj], __half2float(w[p + half_dim])), rms);
-          dst[p] = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p])));
-          dst[p + half_dim] = __float2half_rn(__fadd_rn(__fmul_rn(x0, sn[p]), __fmul_rn(x1, cs[p])));
-        }
+      for (int j = 0; j < pj; j++) {
+        const int p = lane + 32 * j;
+        const float x0 = __fdiv_rn(__fmul_rn(x[j], w[p]), rms);
+        const float x1 = __fdiv_rn(__fmul_rn(x[j + pj], w[p + half_dim]), rms);
+        dst[p] = __float2half_rn(__fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p])));
+        dst[p + half_dim] = __float2half_rn(__fadd_rn(__fmul_rn(x0, sn[p]), __fmul_rn(x1, cs[p])));
       }
     } else {
       dst = v_cache + ((size_t)pos * nkh + (h - nqh - nkh)) * hd;
 #pragma unroll
-      for (int j = 0; j < 16; j++)
-        if (j < nj) dst[lane + 32 * j] = __float2half_rn(__fdiv_rn(x[j], rms));
+      for (int j = 0; j < NJ; j++) dst[lane + 32 * j] = __float2half_rn(__fdiv_rn(x[j], rms));
     }
   }
   g4a::pdl_launch_dependents();
@@ -337,9 +343,19 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
   const uint32_t heads = num_q_heads + 2 * num_kv_heads;
   if (heads == 0) return G4A_OK;
   const uint32_t warps = heads < (uint32_t)kPrepMaxWarps ? heads : (uint32_t)kPrepMaxWarps;
-  dim3 grid(T);
+  decltype(&prefill_prep_kernel<2>) kern = nullptr;
+  switch (head_dim / 32) {
+    case 2: kern = prefill_prep_kernel<2>; break;
+    case 4: kern = prefill_prep_kernel<4>; break;
+    case 6: kern = prefill_prep_kernel<6>; break;
+    case 8: kern = prefill_prep_kernel<8>; break;
+    case 10: kern = prefill_prep_kernel<10>; break;
+    case 12: kern = prefill_prep_kernel<12>; break;
+    case 14: kern = prefill_prep_kernel<14>; break;
+    default: kern = prefill_prep_kernel<16>; break;
+  }
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_PREP);
-  prefill_prep_kernel<<<grid, warps * 32, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
+  kern<<<T, warps * 32, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
                                                      (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
                                                      (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads,
                                                      (int)head_dim, eps, start_pos,
