@@ -356,10 +356,9 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
   }
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_PREP);
   kern<<<T, warps * 32, 0, ctx->stream>>>(q, k, v, (const __half*)q_norm_w, (const __half*)k_norm_w,
-                                                     (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
-                                                     (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads,
-                                                     (int)head_dim, eps, start_pos,
-                                                     make_rope_pow(theta, head_dim), apply_divisor);
+                                          (const __half*)rope_freqs, (__half*)q16_out, (__half*)k_cache,
+                                          (__half*)v_cache, (int)num_q_heads, (int)num_kv_heads, (int)head_dim, eps,
+                                          start_pos, make_rope_pow(theta, head_dim), apply_divisor);
   return g4a_check_launch("prefill_prep_kernel");
 }
 
