@@ -38,8 +38,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 // grid = num_q_heads CTAs of 256 threads.  CTA b pushes this rank's partial to ranks b, b + nqh,
 // ...; every CTA then waits for all flags and merges head b.
-__global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, PeerBufs peers, int world, int rank,
-                                                             uint32_t seq, int nqh, int hd, float* out, int* err) {
+// (`peers` stays in parameter space: __grid_constant__ lets peers.buf[dst] index it directly.)
+__global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, const __grid_constant__ PeerBufs peers,
+                                                             int world, int rank, uint32_t seq, int nqh, int hd,
+                                                             float* out, int* err) {
   const int tid = threadIdx.x;
   const int pf = nqh * (hd + 2);  // floats per partial
   const int ps = (pf + 3) & ~3;   // slot stride (16-byte aligned slots)
