@@ -411,8 +411,10 @@ def run_ours(args):
         line["batched_paged"] = run_batched(ctx, torch, rank, world, dist)
         line["splitkv_1m"] = run_splitkv(ctx, torch, rank, world, dist)
         pf = run_prefill(ctx, torch)
+        pj = run_projections(ctx, torch)
         if rank == 0:
             line["prefill"] = pf
+            line["projections"] = pj
     if rank == 0 and world == 1 and not args.no_sweep:
         line["sweep"] = run_sweep(ctx, torch, args)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -668,6 +670,93 @@ def run_prefill(ctx, torch):
         fl = synth.prefill_flops(T, W)
         res[name] = {"attn_us": us, "tflops": fl / (us * 1e-6) / 1e12, "frac_of_peak": fl / (us * 1e-6) / 1e12 / bf16,
                      "prep_plus_attn_us": us_both, "flops": fl}
+    return res
+
+
+def run_projections(ctx, torch):
+    """The projection GEMVs on either side of attention (src/engine.ts:2043-2053 'attn.linearQKV',
+    :2096 'attn.linearOut') in the reference's three weight modes: per Gemma 4 E2B sliding
+    layer, Q/K/V of the 1536-wide normed hidden state in one grouped launch (2048 + 256 + 256
+    rows), then the O projection (1536 rows x 2048).  R layers' weights are rotated so they
+    exceed L2; one step of R layers is a CUDA graph.  Plus one lm-head sized matrix (262144 x
+    1536, src/engine.ts lmHead) for the streaming rate.  Weight contents are random bits of the
+    right layout (timing does not depend on them); bytes = weight + scales + input + output."""
+    from g4attn import _lib
+
+    hbm, _, kind = peaks()
+    H, Q, KV = 1536, NQH * HD, NKH * HD
+    res = {"config": "Gemma 4 E2B sliding layer: QKV (one grouped launch) + O projection per layer; "
+                     "lm_head 262144 x 1536", "peak_gbs": hbm, "peak_kind": kind}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+
+    def make(fmt, M, N):
+        n = M * N
+        if fmt == _lib.WEIGHT_F16:
+            return (torch.randn(n, generator=g, device="cuda") * 0.05).half(), None, 2 * n
+        if fmt == _lib.WEIGHT_Q8:
+            w = torch.randint(-2**31, 2**31 - 1, (n // 4,), generator=g, device="cuda", dtype=torch.int32)
+            sc = (torch.rand(n // 32, generator=g, device="cuda") * 1e-3).half()
+            return w, sc, n + 2 * (n // 32)
+        w = torch.randint(-2**31, 2**31 - 1, (n // 8,), generator=g, device="cuda", dtype=torch.int32)
+        sc = (torch.rand(n // 16, generator=g, device="cuda") * 1e-2).half()
+        return w, sc, n // 2 + 2 * (n // 16)
+
+    x = torch.randn(H, generator=g, device="cuda")
+    a = torch.randn(Q, generator=g, device="cuda")
+    q, k, v, o = (torch.empty(n, device="cuda") for n in (Q, KV, KV, H))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for name, fmt in (("f16", _lib.WEIGHT_F16), ("q8", _lib.WEIGHT_Q8), ("q4k", _lib.WEIGHT_Q4K)):
+        one = [make(fmt, Q, H), make(fmt, KV, H), make(fmt, KV, H), make(fmt, H, Q)]
+        per_layer = sum(b for (_, _, b) in one) + 4 * (H + Q) * 2
+        R = max(2, min(64, math.ceil(3 * L2_BYTES / per_layer)))
+        layers = [one] + [[make(fmt, M, N) for (M, N) in ((Q, H), (KV, H), (KV, H), (H, Q))] for _ in range(R - 1)]
+
+        def step():
+            for (wq, wk, wv, wo) in layers:
+                ctx.matmul_group(fmt, x, H, [(wq[0], wq[1], q, Q), (wk[0], wk[1], k, KV), (wv[0], wv[1], v, KV)])
+                ctx.matmul(fmt, a, wo[0], wo[1], o, M=H, N=Q)
+
+        step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ctx.set_stream(s.cuda_stream)
+            with torch.cuda.graph(graph, stream=s):
+                step()
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        n = 50
+        e0.record()
+        for _ in range(n):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (n * R)
+        gbs = per_layer / (us * 1e-6) / 1e9
+        # lm-head sized matrix: one launch streams the whole weight
+        M = 262144
+        w, sc, wb = make(fmt, M, H)
+        out = torch.empty(M, device="cuda")
+        for _ in range(3):
+            ctx.matmul(fmt, x, w, sc, out, M=M, N=H)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(10):
+            ctx.matmul(fmt, x, w, sc, out, M=M, N=H)
+        e1.record()
+        torch.cuda.synchronize()
+        us_lm = e0.elapsed_time(e1) * 1e3 / 10
+        lm_bytes = wb + 4 * (H + M)
+        res[name] = {"layer_us": us, "layer_bytes": per_layer, "layer_GB/s": gbs, "layer_frac_of_hbm": gbs / hbm,
+                     "layers_rotated": R, "lm_head_us": us_lm, "lm_head_GB/s": lm_bytes / (us_lm * 1e-6) / 1e9,
+                     "lm_head_frac_of_hbm": lm_bytes / (us_lm * 1e-6) / 1e9 / hbm}
+        del graph, layers, one, w, sc, out
+        torch.cuda.empty_cache()
     return res
 
 

@@ -64,7 +64,7 @@ g4a_status g4a_ensure_workspace(g4a_ctx* ctx, size_t bytes) {
 
 const char* const g4a_prof_names[G4A_PROF_NUM_LABELS] = {
     "norm_rope", "rms_norm_no_weight", "kv_store", "decode_prep", "decode_splitkv",
-    "decode_merge", "decode_generic", "lse_merge", "prefill_prep", "prefill_attn"};
+    "decode_merge", "decode_generic", "lse_merge", "prefill_prep", "prefill_attn", "matmul"};
 
 static cudaEvent_t prof_event(g4a_ctx* ctx) {
   if (!ctx->prof_free.empty()) {

@@ -24,6 +24,7 @@ enum g4a_prof_label : int {
   G4A_PROF_LSE_MERGE,
   G4A_PROF_PREFILL_PREP,
   G4A_PROF_PREFILL_ATTN,
+  G4A_PROF_MATMUL,
   G4A_PROF_NUM_LABELS
 };
 extern const char* const g4a_prof_names[G4A_PROF_NUM_LABELS];

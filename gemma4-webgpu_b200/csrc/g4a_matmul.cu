@@ -1,0 +1,378 @@
+// Projection GEMVs around attention: out[m] = sum_k W[m, k] * input[k] with the weight in the
+// reference's f16, Q8 or 4-bit block-affine storage (shaders/matmul_quant.wgsl,
+// matmul_quant_mr4.wgsl, matmul_q8.wgsl, matmul_q8_mr.wgsl, matmul_q4k.wgsl, matmul_q4k_mr.wgsl;
+// dispatched at src/engine.ts:2043-2053 and :2096).
+//
+// Arithmetic order.  Every one of those shaders computes a row with a 256-thread workgroup:
+// thread t sums term(k) for k = t, t + 256, t + 512, ... in that order from 0.0, then the
+// partials fold with `for stride = 128; stride > 0; stride >>= 1: p[t] += p[t + stride]`
+// (e.g. matmul_quant.wgsl:30-50, matmul_q8_mr.wgsl:49-85).  The per-element terms are
+//   f16 : f32(w) * x                          (matmul_quant.wgsl:34)
+//   Q8  : (f32(q) * f32(scale)) * x            (matmul_q8.wgsl:49, matmul_q8_mr.wgsl:58-61)
+//   Q4K : (f32(scale) * f32(nib) + f32(min)) * x (matmul_q4k.wgsl:54, matmul_q4k_mr.wgsl:74-81)
+// with every product and sum rounded separately (no contraction).  Here one warp computes a
+// row: lane l plays the eight workgroup threads t = 8l .. 8l+7, so one 16-byte (f16), 8-byte
+// (Q8) or 4-byte (Q4K) load per lane per 256-element step brings the lane exactly its threads'
+// elements, and a warp load is one contiguous 512 / 256 / 128-byte run of the row.  The tree
+// levels 128 .. 8 pair thread t with t + stride = 8(l + stride/8) + e, i.e. lane l + stride/8
+// with the same e: five shuffle levels; levels 4, 2, 1 are lane-local in lane 0.  The result
+// is bit-identical to the shader's order.  The f16 path for N % 8 != 0 (or an unaligned
+// weight) uses the other natural layout, threads t = l + 32e, with scalar 2-byte loads.
+//
+// Roofline: HBM-bound streaming of the weight (2 / 1.0625 / 0.625 bytes per element); the
+// input vector is staged once per CTA in shared memory.  The kernel waits for the previous
+// kernel (programmatic dependent launch) only before it reads `input`: the weight does not
+// depend on it, so each warp loads its first row's weights before the wait.
+#include <cuda_fp16.h>
+
+#include "g4a_internal.cuh"
+
+namespace {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr uint32_t kMaxGemvN = 49152;  // input staged in shared memory (192 KB)
+
+struct GemvJob {
+  const void* w;
+  const __half* s;
+  float* out;
+  uint32_t M;
+  uint32_t row0;  // first virtual row of this job
+};
+struct GemvJobs {
+  GemvJob j[G4A_MATMUL_MAX_JOBS];
+  int n;
+  uint32_t rows;  // sum of M
+};
+
+// Streaming loads of the (read-only, read-once) weight.  Not volatile: the compiler may batch
+// them ahead of the arithmetic that consumes them.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 v;
+  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_stream4(const void* p) {
+  uint32_t v;
+  asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Byte i (0..3) of `w` as the float 2^23 + byte, built by one byte permute: the float's low
+// byte is the data byte and its top byte is 0x4B (2^23 has exponent byte 0x4B, mantissa 0), so
+// subtracting the bias is exact and gives small integers without the conversion unit.
+template <int I>
+__device__ __forceinline__ float byte_biased(uint32_t w) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)I));
+}
+
+__device__ __forceinline__ const GemvJob& job_of(const GemvJobs& jobs, uint32_t r, uint32_t& m) {
+  int q = 0;
+#pragma unroll
+  for (int i = 1; i < G4A_MATMUL_MAX_JOBS; i++)
+    if (i < jobs.n && r >= jobs.j[i].row0) q = i;
+  m = r - jobs.j[q].row0;
+  return jobs.j[q];
+}
+
+// Weight bytes of the 256-element step j of row m as seen by `lane`.
+template <uint32_t FMT>
+__device__ __forceinline__ const void* step_ptr(const GemvJob& jb, uint32_t m, uint32_t N, uint32_t j, int lane) {
+  const size_t k = (size_t)m * N + 256u * j + 8u * (uint32_t)lane;  // first element of the lane
+  if constexpr (FMT == G4A_WEIGHT_F16) return reinterpret_cast<const __half*>(jb.w) + k;
+  if constexpr (FMT == G4A_WEIGHT_Q8) return reinterpret_cast<const uint8_t*>(jb.w) + k;
+  return reinterpret_cast<const uint32_t*>(jb.w) + k / 8;
+}
+
+// One 256-element step of a row as one lane sees it: its eight weights (and their scales).
+template <uint32_t FMT>
+struct StepRaw;
+template <>
+struct StepRaw<G4A_WEIGHT_F16> {
+  uint4 w;
+};
+template <>
+struct StepRaw<G4A_WEIGHT_Q8> {
+  uint2 w;
+  __half sc;
+};
+template <>
+struct StepRaw<G4A_WEIGHT_Q4K> {
+  uint32_t w;
+  __half sc, mn;
+};
+// Steps whose loads are issued together before any of them is consumed: 8 steps hold a whole
+// row of the reference's projections (N <= 2048) in one round trip.
+constexpr int kStepBatch = 8;
+
+template <uint32_t FMT>
+__device__ __forceinline__ StepRaw<FMT> load_step(const GemvJob& jb, uint32_t m, uint32_t N, uint32_t j, int lane) {
+  StepRaw<FMT> r;
+  const uint32_t k0 = 256u * j + 8u * (uint32_t)lane;
+  if constexpr (FMT == G4A_WEIGHT_F16) {
+    r.w = ld_stream16(step_ptr<FMT>(jb, m, N, j, lane));
+  } else if constexpr (FMT == G4A_WEIGHT_Q8) {
+    r.w = ld_stream8(step_ptr<FMT>(jb, m, N, j, lane));
+    // the lane's 8 elements lie in one 32-element block: (m N + k0) / 32
+    r.sc = __ldg(jb.s + (size_t)m * (N / 32u) + (k0 >> 5));
+  } else {
+    r.w = ld_stream4(step_ptr<FMT>(jb, m, N, j, lane));
+    // super-block j = k0 >> 8, sub-block (k0 & 255) >> 5 = lane / 4
+    const __half* meta = jb.s + (size_t)m * (N / 256u) * 16u + 16u * j;
+    r.sc = __ldg(meta + (lane >> 2));
+    r.mn = __ldg(meta + 8 + (lane >> 2));
+  }
+  return r;
+}
+
+// acc[e] += term(element 256 j + 8 lane + e) for the lane's eight threads.
+template <uint32_t FMT>
+__device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, int lane, const float* xs,
+                                             float (&acc)[8]) {
+  const uint32_t k0 = 256u * j + 8u * (uint32_t)lane;
+  const float4 xa = *reinterpret_cast<const float4*>(xs + k0);
+  const float4 xb = *reinterpret_cast<const float4*>(xs + k0 + 4);
+  const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  if constexpr (FMT == G4A_WEIGHT_F16) {
+    const uint32_t w4[4] = {r.w.x, r.w.y, r.w.z, r.w.w};
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const __half h = __ushort_as_half((unsigned short)(w4[e / 2] >> (16 * (e & 1))));
+      acc[e] = __fadd_rn(acc[e], __fmul_rn(__half2float(h), x[e]));
+    }
+  } else if constexpr (FMT == G4A_WEIGHT_Q8) {
+    // int8 q as the byte u = q + 128 (flip the sign bit of every byte): 2^23 + u - (2^23 + 128)
+    const float sc = __half2float(r.sc);
+    const uint32_t u0 = r.w.x ^ 0x80808080u, u1 = r.w.y ^ 0x80808080u;
+    const float q[8] = {byte_biased<0>(u0), byte_biased<1>(u0), byte_biased<2>(u0), byte_biased<3>(u0),
+                        byte_biased<0>(u1), byte_biased<1>(u1), byte_biased<2>(u1), byte_biased<3>(u1)};
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+      acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(__fsub_rn(q[e], 8388736.0f), sc), x[e]));
+  } else {
+    // Nibbles 0, 2, 4, 6 are the bytes of `lo`, nibbles 1, 3, 5, 7 those of `hi`.
+    const uint32_t lo = r.w & 0x0F0F0F0Fu, hi = (r.w >> 4) & 0x0F0F0F0Fu;
+    const float nb[8] = {byte_biased<0>(lo), byte_biased<0>(hi), byte_biased<1>(lo), byte_biased<1>(hi),
+                         byte_biased<2>(lo), byte_biased<2>(hi), byte_biased<3>(lo), byte_biased<3>(hi)};
+    const float sc = __half2float(r.sc), mn = __half2float(r.mn);
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      // The shader's RN(RN(scale * nib) + min) is one fused multiply-add here: scale is an f16
+      // value and nib an integer below 16, so their product has at most 15 significant bits
+      // within the f32 normal range and is exact; the fma's single rounding is then the sum's.
+      const float wv = __fmaf_rn(sc, __fsub_rn(nb[e], 8388608.0f), mn);
+      acc[e] = __fadd_rn(acc[e], __fmul_rn(wv, x[e]));
+    }
+  }
+}
+
+// The 256-thread tree for threads t = 8 lane + e; lane 0 returns p[0].
+__device__ __forceinline__ float tree_8l_e(float (&acc)[8]) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1)  // strides 128, 64, 32, 16, 8
+#pragma unroll
+    for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], __shfl_down_sync(0xffffffffu, acc[e], off));
+#pragma unroll
+  for (int e = 0; e < 4; e++) acc[e] = __fadd_rn(acc[e], acc[e + 4]);  // stride 4
+  acc[0] = __fadd_rn(acc[0], acc[2]);                                   // stride 2
+  acc[1] = __fadd_rn(acc[1], acc[3]);
+  return __fadd_rn(acc[0], acc[1]);                                     // stride 1
+}
+
+// Stage input[0, N) into shared memory (after the PDL wait).
+__device__ __forceinline__ void stage_input(const float* __restrict__ x, uint32_t N, float* xs, uint32_t padded) {
+  const int t = threadIdx.x;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (N & 3u) == 0) {
+    for (uint32_t i = t; i < N / 4; i += kGemvThreads)
+      reinterpret_cast<float4*>(xs)[i] = __ldg(reinterpret_cast<const float4*>(x) + i);
+  } else {
+    for (uint32_t i = t; i < N; i += kGemvThreads) xs[i] = __ldg(x + i);
+  }
+  for (uint32_t i = N + t; i < padded; i += kGemvThreads) xs[i] = 0.f;
+}
+
+// Vector path: N % 8 == 0 (Q8: N % 32, Q4K: N % 256), 16-byte aligned weights.
+template <uint32_t FMT>
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __restrict__ x, uint32_t N,
+                                                            const __grid_constant__ GemvJobs jobs) {
+  extern __shared__ float4 gemv_smem[];
+  float* xs = reinterpret_cast<float*>(gemv_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t steps = (N + 255u) / 256u;
+  const uint32_t stride = gridDim.x * kGemvWarps;
+  // A lane's steps: all 256-element steps, and the partial last one where its 8 elements lie
+  // below N.  Threads past N keep a zero partial, as in the shader (their loop never runs).
+  const uint32_t mine = steps - ((steps > N / 256u && 256u * (steps - 1) + 8u * lane >= N) ? 1u : 0u);
+  constexpr int B = kStepBatch;
+  // Software pipeline over a warp's rows (Q8, Q4K: a batch is 24-32 registers): the first
+  // batch of the next row is loaded while the current row is summed.  f16 batches are twice as
+  // large, and two of them would halve the CTAs an SM holds, so f16 loads each row's batch at
+  // the row's start.  The weight does not depend on the preceding kernel, so the first row's
+  // batch is loaded before the programmatic-launch wait, overlapping that kernel's tail.
+  constexpr bool kPipe = FMT != G4A_WEIGHT_F16;
+  StepRaw<FMT> nxt[B];
+  uint32_t r = blockIdx.x * kGemvWarps + warp;
+  auto load_batch = [&](StepRaw<FMT>(&raw)[B], uint32_t row, uint32_t j0) {
+    uint32_t m;
+    const GemvJob& jb = job_of(jobs, row, m);
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if (j0 + u < mine) raw[u] = load_step<FMT>(jb, m, N, j0 + u, lane);
+  };
+  if (r < jobs.rows) load_batch(nxt, r, 0);
+  g4a::pdl_wait_primary();  // `input` is written by the preceding kernel
+  stage_input(x, N, xs, steps * 256u);
+  __syncthreads();
+  g4a::pdl_launch_dependents();
+  // Sums row `row` whose first batch is in `raw` (the array is reused for later batches).
+  auto sum_row = [&](StepRaw<FMT>(&raw)[B], uint32_t row) {
+    uint32_t m;
+    const GemvJob& jb = job_of(jobs, row, m);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if ((uint32_t)u < mine) consume_step<FMT>(raw[u], u, lane, xs, acc);
+    for (uint32_t j = B; j < mine; j += B) {  // rows longer than one batch
+      load_batch(raw, row, j);
+#pragma unroll
+      for (int u = 0; u < B; u++)
+        if (j + u < mine) consume_step<FMT>(raw[u], j + u, lane, xs, acc);
+    }
+    const float v = tree_8l_e(acc);
+    if (lane == 0) jb.out[m] = v;
+  };
+  if constexpr (kPipe) {
+    for (; r < jobs.rows; r += stride) {
+      StepRaw<FMT> cur[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) cur[u] = nxt[u];
+      if (r + stride < jobs.rows) load_batch(nxt, r + stride, 0);
+      sum_row(cur, r);
+    }
+  } else {
+    for (bool first = true; r < jobs.rows; r += stride, first = false) {
+      if (!first) load_batch(nxt, r, 0);
+      sum_row(nxt, r);
+    }
+  }
+}
+
+// Scalar f16 path for any N and 2-byte aligned weights: threads t = lane + 32 e.
+__global__ void __launch_bounds__(kGemvThreads) gemv_f16_scalar_kernel(const float* __restrict__ x, uint32_t N,
+                                                                       const __grid_constant__ GemvJobs jobs) {
+  extern __shared__ float4 gemv_smem[];
+  float* xs = reinterpret_cast<float*>(gemv_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  g4a::pdl_wait_primary();
+  stage_input(x, N, xs, N);
+  __syncthreads();
+  g4a::pdl_launch_dependents();
+  for (uint32_t r = blockIdx.x * kGemvWarps + warp; r < jobs.rows; r += gridDim.x * kGemvWarps) {
+    uint32_t m;
+    const GemvJob& jb = job_of(jobs, r, m);
+    const __half* w = reinterpret_cast<const __half*>(jb.w) + (size_t)m * N;
+    float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (uint32_t base = 0; base < N; base += 256u) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const uint32_t k = base + (uint32_t)lane + 32u * e;
+        if (k < N) p[e] = __fadd_rn(p[e], __fmul_rn(__half2float(w[k]), xs[k]));
+      }
+    }
+    // strides 128, 64, 32 pair e with e + 4, e + 2, e + 1 in the same lane
+#pragma unroll
+    for (int e = 0; e < 4; e++) p[e] = __fadd_rn(p[e], p[e + 4]);
+    p[0] = __fadd_rn(p[0], p[2]);
+    p[1] = __fadd_rn(p[1], p[3]);
+    float v = __fadd_rn(p[0], p[1]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, off));
+    if (lane == 0) jb.out[m] = v;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+g4a_status g4a_matmul_group(g4a_ctx* ctx, uint32_t weight_format, const float* input, uint32_t N,
+                            const g4a_matmul_job* jobs, uint32_t num_jobs) {
+  G4A_CHECK_CTX(ctx);
+  if (weight_format > G4A_WEIGHT_Q4K) return g4a_fail(G4A_EINVAL, "g4a_matmul: unknown weight_format %u", weight_format);
+  if (num_jobs == 0 || num_jobs > G4A_MATMUL_MAX_JOBS || !jobs)
+    return g4a_fail(G4A_EINVAL, "g4a_matmul_group: num_jobs %u not in [1, %d]", num_jobs, G4A_MATMUL_MAX_JOBS);
+  if (N > kMaxGemvN) return g4a_fail(G4A_EINVAL, "g4a_matmul: N %u > %u", N, kMaxGemvN);
+  if (weight_format == G4A_WEIGHT_Q8 && (N % 32u) != 0)
+    return g4a_fail(G4A_EINVAL, "g4a_matmul: Q8 needs N %% 32 == 0 (N = %u)", N);
+  if (weight_format == G4A_WEIGHT_Q4K && (N % 256u) != 0)
+    return g4a_fail(G4A_EINVAL, "g4a_matmul: Q4K needs N %% 256 == 0 (N = %u)", N);
+  GemvJobs J = {};
+  bool vec = (N % 8u) == 0;
+  uint64_t rows = 0;
+  for (uint32_t i = 0; i < num_jobs; i++) {
+    const g4a_matmul_job& s = jobs[i];
+    if (s.M == 0) continue;
+    if (!s.weight || !s.out) return g4a_fail(G4A_EINVAL, "g4a_matmul: job %u: null weight or out", i);
+    if (weight_format != G4A_WEIGHT_F16 && !s.scales)
+      return g4a_fail(G4A_EINVAL, "g4a_matmul: job %u: null scales", i);
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(s.weight);
+    if (weight_format == G4A_WEIGHT_F16) {
+      if (wa & 1u) return g4a_fail(G4A_EINVAL, "g4a_matmul: job %u: f16 weight not 2-byte aligned", i);
+      if (wa & 15u) vec = false;
+    } else if (wa & 15u) {
+      return g4a_fail(G4A_EINVAL, "g4a_matmul: job %u: quantised weight not 16-byte aligned", i);
+    }
+    if (s.scales && (reinterpret_cast<uintptr_t>(s.scales) & 1u))
+      return g4a_fail(G4A_EINVAL, "g4a_matmul: job %u: scales not 2-byte aligned", i);
+    J.j[J.n] = GemvJob{s.weight, reinterpret_cast<const __half*>(s.scales), s.out, s.M, (uint32_t)rows};
+    J.n++;
+    rows += s.M;
+  }
+  if (rows == 0) return G4A_OK;
+  if (rows > 0xffffffffull - 2u * 148u * kGemvWarps) return g4a_fail(G4A_EINVAL, "g4a_matmul: too many rows");
+  if (!input) return g4a_fail(G4A_EINVAL, "g4a_matmul: null input");
+  J.rows = (uint32_t)rows;
+  const uint32_t padded = (N + 255u) / 256u * 256u;
+  const size_t smem = (size_t)(vec ? padded : (N ? N : 1u)) * sizeof(float);
+  // Up to 8 CTAs of 8 warps per SM, one row per warp per pass.
+  const uint64_t want = (rows + kGemvWarps - 1) / kGemvWarps;
+  const uint64_t cap = (uint64_t)ctx->num_sms * 8u;
+  const dim3 grid((unsigned)(want < cap ? want : cap));
+  g4a_prof_scope ps(ctx, G4A_PROF_MATMUL);
+  cudaError_t e;
+  if (!vec) {
+    if (smem > 48u * 1024u) {
+      const cudaError_t a =
+          cudaFuncSetAttribute(gemv_f16_scalar_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (a != cudaSuccess) return g4a_cuda_fail(a, "cudaFuncSetAttribute(gemv)");
+    }
+    e = g4a_launch(gemv_f16_scalar_kernel, grid, dim3(kGemvThreads), smem, ctx->stream, true, input, N, J);
+  } else {
+    auto kern = weight_format == G4A_WEIGHT_F16 ? gemv_kernel<G4A_WEIGHT_F16>
+                : weight_format == G4A_WEIGHT_Q8 ? gemv_kernel<G4A_WEIGHT_Q8>
+                                                 : gemv_kernel<G4A_WEIGHT_Q4K>;
+    if (smem > 48u * 1024u) {
+      const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (a != cudaSuccess) return g4a_cuda_fail(a, "cudaFuncSetAttribute(gemv)");
+    }
+    e = g4a_launch(kern, grid, dim3(kGemvThreads), smem, ctx->stream, true, input, N, J);
+  }
+  if (e != cudaSuccess) return g4a_cuda_fail(e, "launch gemv");
+  return G4A_OK;
+}
+
+g4a_status g4a_matmul(g4a_ctx* ctx, uint32_t weight_format, const float* input, const void* weight,
+                      const uint16_t* scales, float* out, uint32_t M, uint32_t N) {
+  const g4a_matmul_job job = {weight, scales, out, M};
+  return g4a_matmul_group(ctx, weight_format, input, N, &job, 1);
+}
+
+}  // extern "C"

@@ -12,6 +12,7 @@ from __future__ import annotations
 import ctypes
 from ctypes import c_void_p
 
+from . import _lib
 from ._lib import G4AError, call, exported_symbols, load  # noqa: F401
 
 __all__ = ["Context", "G4AError", "load", "exported_symbols", "version"]
@@ -269,6 +270,25 @@ class Context:
         arr = (c_void_p * len(rank_buffers))(*[c_void_p(b) for b in rank_buffers])
         call("g4a_splitkv_exchange_merge", self._h, _ptr(part), arr, len(rank_buffers), int(rank), int(seq),
              num_q_heads, head_dim, _ptr(out))
+
+    # ---------------------------------------------------------------- projections
+    def matmul(self, weight_format: int, x, weight, scales, out, *, M: int, N: int) -> None:
+        """out[m] = sum_k W[m, k] x[k] (g4a_matmul): the Q/K/V and O projections
+        (shaders/matmul_quant*.wgsl, matmul_q8*.wgsl, matmul_q4k*.wgsl).  weight_format is
+        _lib.WEIGHT_F16 / WEIGHT_Q8 / WEIGHT_Q4K; the packing is g4attn.quant's."""
+        import torch
+
+        _check(x, "input", torch.float32, None, self.device)
+        _check(out, "out", torch.float32, None, self.device)
+        call("g4a_matmul", self._h, int(weight_format), _ptr(x), _ptr(weight), _ptr(scales), _ptr(out), int(M),
+             int(N))
+
+    def matmul_group(self, weight_format: int, x, N: int, jobs) -> None:
+        """Several matrices over one input in one launch (g4a_matmul_group), as the reference's
+        'attn.linearQKV' pass; jobs = [(weight, scales, out, M), ...] (at most 4)."""
+        arr = (_lib.MatmulJob * len(jobs))(
+            *[_lib.MatmulJob(_ptr(w).value, _ptr(sc).value, _ptr(o).value, int(m)) for (w, sc, o, m) in jobs])
+        call("g4a_matmul_group", self._h, int(weight_format), _ptr(x), int(N), arr, len(jobs))
 
     # ---------------------------------------------------------------- prefill
     def prefill_qkv_prep(self, q, k, v, q_norm_w, k_norm_w, rope_freqs, q16_out, k_cache, v_cache, *, T,

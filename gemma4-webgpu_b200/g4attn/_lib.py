@@ -35,6 +35,16 @@ class G4AError(RuntimeError):
         super().__init__(f"{func}: {self.status_name}: {message}")
 
 
+WEIGHT_F16, WEIGHT_Q8, WEIGHT_Q4K = 0, 1, 2  # G4A_WEIGHT_* of g4a_matmul
+MATMUL_MAX_JOBS = 4
+
+
+class MatmulJob(ctypes.Structure):
+    """g4a_matmul_job: one matrix of a g4a_matmul_group call."""
+
+    _fields_ = [("weight", c_void_p), ("scales", c_void_p), ("out", c_void_p), ("M", c_uint32)]
+
+
 # (name, argtypes) for every g4a_status entry point.
 _u32 = c_uint32
 _f = c_float
@@ -71,6 +81,8 @@ SIGNATURES: dict[str, list] = {
     "g4a_ipc_open_handle": [_p, _p, POINTER(c_void_p)],
     "g4a_ipc_close_handle": [_p, _p],
     "g4a_splitkv_exchange_merge": [_p, _p, POINTER(c_void_p), _u32, _u32, _u32, _u32, _u32, _p],
+    "g4a_matmul": [_p, _u32, _p, _p, _p, _p, _u32, _u32],
+    "g4a_matmul_group": [_p, _u32, _p, _u32, POINTER(MatmulJob), _u32],
 }
 EXTRA_SYMBOLS = {"g4a_last_error": ([], c_char_p), "g4a_version": ([], c_char_p),
                  "g4a_get_stream": ([c_void_p], c_void_p),

@@ -97,7 +97,7 @@ g4a_status g4a_reserve_workspace(g4a_ctx* ctx, uint32_t max_batch, uint32_t head
 /* Per-kernel profiler: when enabled, every kernel launch is bracketed by CUDA events and its
  * device time is summed per label ("norm_rope", "rms_norm_no_weight", "kv_store",
  * "decode_prep", "decode_splitkv", "decode_merge", "decode_generic", "lse_merge",
- * "prefill_prep", "prefill_attn").  Counterpart of the reference's per-pass timestamp
+ * "prefill_prep", "prefill_attn", "matmul").  Counterpart of the reference's per-pass timestamp
  * queries (src/engine.ts:3208-3285, src/diagnostics/profile.ts:48-132).  Reading waits for
  * the context's stream.  Leave it off for timing whole steps: the events serialise launches. */
 g4a_status g4a_profile_enable(g4a_ctx* ctx, int enable);
@@ -267,6 +267,51 @@ g4a_status g4a_ipc_close_handle(g4a_ctx* ctx, void* dptr);
 g4a_status g4a_splitkv_exchange_merge(g4a_ctx* ctx, const float* part, void* const* rank_buffers,
                                       uint32_t world, uint32_t rank, uint32_t seq,
                                       uint32_t num_q_heads, uint32_t head_dim, float* out);
+
+/* ------------------------------------------------------------------ projections (GEMV) */
+
+/* The matrix-vector products on either side of attention: the Q/K/V projections of the
+ * normed hidden state (src/engine.ts:2043-2053, pass 'attn.linearQKV') and the output
+ * projection of the attention output (src/engine.ts:2096, pass 'attn.linearOut').
+ * out[m] = sum_k W[m, k] * input[k] for an [M, N] weight in one of the reference's three
+ * storage modes (`weightQuant`, src/engine.ts:107):
+ *   G4A_WEIGHT_F16 : weight = f16 [M, N] row-major.  Replaces shaders/matmul_quant.wgsl and
+ *                    matmul_quant_mr4.wgsl (bindings input, weight, output, Params {M, N}).
+ *   G4A_WEIGHT_Q8  : weight = int8 [M, N] packed 4 per uint32 (element k of row m is byte
+ *                    (m*N + k) % 4 of word (m*N + k) / 4), scales = f16 [M, N/32], one per
+ *                    32-element block; value = int8 * scale.  N % 32 == 0.  Replaces
+ *                    shaders/matmul_q8.wgsl / matmul_q8_mr.wgsl (bindings input, qweight,
+ *                    qscale, output, Params {M, N}); layout made by createQ8Buffers
+ *                    (src/engine.ts:638-674).
+ *   G4A_WEIGHT_Q4K : weight = 4-bit [M, N] packed 8 per uint32 (nibble (m*N + k) % 8 of word
+ *                    (m*N + k) / 8), scales = the f16 meta [M, N/256, 16]: for each
+ *                    256-element super-block 8 sub-block scales then 8 sub-block mins (32
+ *                    elements per sub-block); value = scale * nibble + min.  N % 256 == 0.
+ *                    Replaces shaders/matmul_q4k.wgsl / matmul_q4k_mr.wgsl; layout made by
+ *                    createQ4KBuffers (src/engine.ts:699-739).
+ * Every output is bit-identical to the shaders' arithmetic without contraction: the
+ * 256-thread partial sums over k = t, t + 256, ... in order, then the stride-halving tree.
+ * input and out are f32 device arrays; the weight pointer must be 16-byte aligned for Q8 and
+ * Q4K (F16 takes any 2-byte aligned pointer and any N). */
+#define G4A_WEIGHT_F16 0u
+#define G4A_WEIGHT_Q8 1u
+#define G4A_WEIGHT_Q4K 2u
+g4a_status g4a_matmul(g4a_ctx* ctx, uint32_t weight_format, const float* input, const void* weight,
+                      const uint16_t* scales, float* out, uint32_t M, uint32_t N);
+
+/* Several matrices over the same input in one launch, as the reference's 'attn.linearQKV'
+ * pass dispatches the Q, K and V matmuls from one bind of the normed hidden state
+ * (src/engine.ts:2045-2052).  1 <= num_jobs <= G4A_MATMUL_MAX_JOBS; all jobs share
+ * weight_format and N; scales may be NULL for G4A_WEIGHT_F16. */
+#define G4A_MATMUL_MAX_JOBS 4
+typedef struct {
+  const void* weight;
+  const uint16_t* scales;
+  float* out;
+  uint32_t M;
+} g4a_matmul_job;
+g4a_status g4a_matmul_group(g4a_ctx* ctx, uint32_t weight_format, const float* input, uint32_t N,
+                            const g4a_matmul_job* jobs, uint32_t num_jobs);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

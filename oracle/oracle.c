@@ -13,6 +13,9 @@
  *   shaders/attn_score.wgsl:15-40                 -> orc_attn_score
  *   shaders/softmax.wgsl:7-46                     -> orc_softmax
  *   shaders/attn_output.wgsl:7-23                 -> orc_attn_output
+ *   shaders/matmul_quant.wgsl, matmul_quant_mr4.wgsl -> orc_matmul_f16
+ *   shaders/matmul_q8.wgsl, matmul_q8_mr.wgsl      -> orc_matmul_q8
+ *   shaders/matmul_q4k.wgsl, matmul_q4k_mr.wgsl    -> orc_matmul_q4k
  * and the dispatch order of src/engine.ts:2061-2094 (v_norm, norm+RoPE, store, score,
  * softmax, output) in orc_decode_chain_f32.
  *
@@ -406,6 +409,72 @@ void orc_prefill_attn_f64(const float* q, const uint16_t* k_cache, const uint16_
   for (uint32_t i = 0; i < T; i++)
     orc_decode_attn_f64(q + i * row, k_cache, v_cache, out + i * row, num_q_heads, num_kv_heads,
                         head_dim, start_pos + i + 1u, scale, sliding_window);
+}
+
+/* ------------------------------------------------------------- projection matmuls */
+
+/* One output row as a 256-thread workgroup of the matmul shaders computes it: thread t
+ * accumulates term(k) for k = t, t + 256, ... from 0.0 in order (acc = acc + term), then
+ * the partials fold with the stride-halving tree; output = p[0].  matmul_quant.wgsl:29-52,
+ * matmul_q8.wgsl:42-66, matmul_q4k.wgsl:41-71 (the _mr variants, matmul_quant_mr4.wgsl:55-89,
+ * matmul_q8_mr.wgsl:49-86 and matmul_q4k_mr.wgsl:54-96, keep the same per-row order). */
+#define ROW_TREE(TERM)                                         \
+  do {                                                         \
+    float p_[WG];                                              \
+    for (uint32_t t = 0; t < WG; t++) {                        \
+      float acc = 0.0f;                                        \
+      for (uint32_t k = t; k < N; k += WG) acc = acc + (TERM); \
+      p_[t] = acc;                                             \
+    }                                                          \
+    for (uint32_t st = WG / 2; st > 0; st >>= 1)               \
+      for (uint32_t t = 0; t < st; t++) p_[t] = p_[t] + p_[t + st]; \
+    out[m] = p_[0];                                            \
+  } while (0)
+
+/* f16 weight [M, N]: term = f32(weight[m N + k]) * input[k]   (matmul_quant.wgsl:34) */
+void orc_matmul_f16(const float* input, const uint16_t* weight, float* out, uint32_t M, uint32_t N) {
+#pragma omp parallel for schedule(static)
+  for (int64_t mm = 0; mm < (int64_t)M; mm++) {
+    const uint32_t m = (uint32_t)mm;
+    const uint16_t* w = weight + (size_t)m * N;
+    ROW_TREE(orc_half_to_float(w[k]) * input[k]);
+  }
+}
+
+/* int8 of the packed word, as unpack_i8 (matmul_q8.wgsl:25-28) */
+static int32_t unpack_i8(uint32_t packed, uint32_t lane) {
+  uint32_t b = (packed >> (lane * 8u)) & 0xffu;
+  return b >= 128u ? (int32_t)b - 256 : (int32_t)b;
+}
+
+/* Q8: term = f32(q) * f32(scale[m N/32 + k/32]) * input[k]   (matmul_q8.wgsl:45-50) */
+void orc_matmul_q8(const float* input, const uint32_t* qweight, const uint16_t* qscale, float* out, uint32_t M,
+                   uint32_t N) {
+  const uint32_t nblocks = N / 32u;
+#pragma omp parallel for schedule(static)
+  for (int64_t mm = 0; mm < (int64_t)M; mm++) {
+    const uint32_t m = (uint32_t)mm;
+    const size_t qb = (size_t)m * N, sb = (size_t)m * nblocks;
+    ROW_TREE((float)unpack_i8(qweight[(qb + k) >> 2], (uint32_t)((qb + k) & 3u)) *
+             orc_half_to_float(qscale[sb + (k >> 5)]) * input[k]);
+  }
+}
+
+/* 4-bit block-affine: nib = nibble (m N + k) % 8 of word (m N + k) / 8; with sb = k / 256 and
+ * sub = (k % 256) / 32, term = (f32(meta[sb*16 + sub]) * f32(nib) + f32(meta[sb*16 + 8 + sub]))
+ * * input[k]   (matmul_q4k.wgsl:44-55) */
+void orc_matmul_q4k(const float* input, const uint32_t* qweight, const uint16_t* qmeta, float* out, uint32_t M,
+                    uint32_t N) {
+  const uint32_t nsblk = N / 256u;
+#pragma omp parallel for schedule(static)
+  for (int64_t mm = 0; mm < (int64_t)M; mm++) {
+    const uint32_t m = (uint32_t)mm;
+    const size_t qb = (size_t)m * N, mb = (size_t)m * nsblk * 16u;
+    ROW_TREE((orc_half_to_float(qmeta[mb + (k >> 8) * 16u + ((k & 255u) >> 5)]) *
+                  (float)((qweight[(qb + k) >> 3] >> (((qb + k) & 7u) * 4u)) & 0xfu) +
+              orc_half_to_float(qmeta[mb + (k >> 8) * 16u + 8u + ((k & 255u) >> 5)])) *
+             input[k]);
+  }
 }
 
 int orc_num_threads(void) {

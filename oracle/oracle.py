@@ -55,6 +55,10 @@ def lib() -> ctypes.CDLL:
         L.orc_decode_attn_f64.argtypes = [f32p, u16p, u16p, f32p, u, u, u, u, c_float, u]
         L.orc_decode_partial_f64.argtypes = [f32p, u16p, u16p, u, u, u, u, u, u, c_float, u, f64p, f64p, f64p]
         L.orc_prefill_attn_f64.argtypes = [f32p, u16p, u16p, f32p, u, u, u, u, u, c_float, u]
+        u32p = POINTER(c_uint32)
+        L.orc_matmul_f16.argtypes = [f32p, u16p, f32p, u, u]
+        L.orc_matmul_q8.argtypes = [f32p, u32p, u16p, f32p, u, u]
+        L.orc_matmul_q4k.argtypes = [f32p, u32p, u16p, f32p, u, u]
         L.orc_num_threads.restype = c_int
         L.orc_set_num_threads.argtypes = [c_int]
         _lib = L
@@ -218,3 +222,23 @@ def decode_numpy_f64(q, k_cache, v_cache, kv_len, window=0, scale=1.0, nkh=1):
         p = np.exp(s - s.max())
         out[h] = (p @ V[:, kvh, :]) / p.sum()
     return out.astype(np.float32)
+
+
+def matmul(weight_format: int, x, weight, scales, M: int, N: int) -> np.ndarray:
+    """out[m] = sum_k W[m, k] x[k] in the reference shaders' order (orc_matmul_*).
+    weight_format 0 = f16 (weight uint16 [M, N]), 1 = Q8 (weight uint32 [M*N/4], scales uint16
+    [M, N/32]), 2 = Q4K (weight uint32 [M*N/8], scales uint16 [M, N/256, 16])."""
+    x, px = _f32(np.asarray(x).reshape(-1))
+    assert x.size >= N
+    out = np.zeros(M, dtype=np.float32)
+    pout = out.ctypes.data_as(POINTER(c_float))
+    w = np.ascontiguousarray(weight).reshape(-1)
+    if weight_format == 0:
+        w, pw = _u16(w.view(np.uint16))
+        lib().orc_matmul_f16(px, pw, pout, M, N)
+    else:
+        w = np.ascontiguousarray(w.view(np.uint32))
+        s, ps = _u16(np.ascontiguousarray(scales).reshape(-1).view(np.uint16))
+        fn = lib().orc_matmul_q8 if weight_format == 1 else lib().orc_matmul_q4k
+        fn(px, w.ctypes.data_as(POINTER(c_uint32)), ps, pout, M, N)
+    return out
