@@ -265,6 +265,76 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __re
   }
 }
 
+// Rows of exactly S full 256-element steps (N = 256 S, S <= 8: every projection of the
+// reference model): a lane's row pointer is formed once and every step is a compile-time
+// offset from it, with no per-step bounds predicate.  Q8 and Q4K load the next row's steps
+// while the current row is summed; f16 (twice the registers per step) loads at the row start.
+template <uint32_t FMT, int S>
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float* __restrict__ x,
+                                                                     const __grid_constant__ GemvJobs jobs) {
+  constexpr uint32_t N = 256u * S;
+  extern __shared__ float4 gemv_smem[];
+  float* xs = reinterpret_cast<float*>(gemv_smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t stride = gridDim.x * kGemvWarps;
+  auto load_row = [&](StepRaw<FMT>(&raw)[S], uint32_t row) {
+    uint32_t m;
+    const GemvJob& jb = job_of(jobs, row, m);
+    if constexpr (FMT == G4A_WEIGHT_F16) {
+      const __half* w = reinterpret_cast<const __half*>(jb.w) + (size_t)m * N + 8u * lane;
+#pragma unroll
+      for (int u = 0; u < S; u++) raw[u].w = ld_stream16(w + 256 * u);
+    } else if constexpr (FMT == G4A_WEIGHT_Q8) {
+      const uint8_t* w = reinterpret_cast<const uint8_t*>(jb.w) + (size_t)m * N + 8u * lane;
+      const __half* sc = jb.s + (size_t)m * (N / 32u) + (lane >> 2);  // block 8 u + lane / 4
+#pragma unroll
+      for (int u = 0; u < S; u++) {
+        raw[u].w = ld_stream8(w + 256 * u);
+        raw[u].sc = __ldg(sc + 8 * u);
+      }
+    } else {
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(jb.w) + (size_t)m * (N / 8u) + lane;
+      const __half* meta = jb.s + (size_t)m * (16u * S) + (lane >> 2);  // super-block u, sub lane / 4
+#pragma unroll
+      for (int u = 0; u < S; u++) {
+        raw[u].w = ld_stream4(w + 32 * u);
+        raw[u].sc = __ldg(meta + 16 * u);
+        raw[u].mn = __ldg(meta + 16 * u + 8);
+      }
+    }
+  };
+  auto sum_row = [&](const StepRaw<FMT>(&raw)[S], uint32_t row) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < S; u++) consume_step<FMT>(raw[u], (uint32_t)u, lane, xs, acc);
+    const float v = tree_8l_e(acc);
+    uint32_t m;
+    const GemvJob& jb = job_of(jobs, row, m);
+    if (lane == 0) jb.out[m] = v;
+  };
+  uint32_t r = blockIdx.x * kGemvWarps + warp;
+  StepRaw<FMT> nxt[S];
+  if (r < jobs.rows) load_row(nxt, r);  // independent of the preceding kernel
+  g4a::pdl_wait_primary();              // `input` is written by the preceding kernel
+  stage_input(x, N, xs, N);
+  __syncthreads();
+  g4a::pdl_launch_dependents();
+  if constexpr (FMT != G4A_WEIGHT_F16) {
+    for (; r < jobs.rows; r += stride) {
+      StepRaw<FMT> cur[S];
+#pragma unroll
+      for (int u = 0; u < S; u++) cur[u] = nxt[u];
+      if (r + stride < jobs.rows) load_row(nxt, r + stride);
+      sum_row(cur, r);
+    }
+  } else {
+    for (bool first = true; r < jobs.rows; r += stride, first = false) {
+      if (!first) load_row(nxt, r);
+      sum_row(nxt, r);
+    }
+  }
+}
+
 // Scalar f16 path for any N and 2-byte aligned weights: threads t = lane + 32 e.
 __global__ void __launch_bounds__(kGemvThreads) gemv_f16_scalar_kernel(const float* __restrict__ x, uint32_t N,
                                                                        const __grid_constant__ GemvJobs jobs) {
@@ -356,14 +426,33 @@ g4a_status g4a_matmul_group(g4a_ctx* ctx, uint32_t weight_format, const float* i
     }
     e = g4a_launch(gemv_f16_scalar_kernel, grid, dim3(kGemvThreads), smem, ctx->stream, true, input, N, J);
   } else {
-    auto kern = weight_format == G4A_WEIGHT_F16 ? gemv_kernel<G4A_WEIGHT_F16>
-                : weight_format == G4A_WEIGHT_Q8 ? gemv_kernel<G4A_WEIGHT_Q8>
-                                                 : gemv_kernel<G4A_WEIGHT_Q4K>;
-    if (smem > 48u * 1024u) {
-      const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (a != cudaSuccess) return g4a_cuda_fail(a, "cudaFuncSetAttribute(gemv)");
+    const uint32_t S = N / 256u;
+    if (N % 256u == 0 && S >= 1 && S <= 8) {
+      using FixedKernel = void (*)(const float*, GemvJobs);
+      static const FixedKernel fixed[3][8] = {
+          {gemv_fixed_kernel<G4A_WEIGHT_F16, 1>, gemv_fixed_kernel<G4A_WEIGHT_F16, 2>,
+           gemv_fixed_kernel<G4A_WEIGHT_F16, 3>, gemv_fixed_kernel<G4A_WEIGHT_F16, 4>,
+           gemv_fixed_kernel<G4A_WEIGHT_F16, 5>, gemv_fixed_kernel<G4A_WEIGHT_F16, 6>,
+           gemv_fixed_kernel<G4A_WEIGHT_F16, 7>, gemv_fixed_kernel<G4A_WEIGHT_F16, 8>},
+          {gemv_fixed_kernel<G4A_WEIGHT_Q8, 1>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 2>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 3>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 4>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 5>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 6>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 7>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 8>},
+          {gemv_fixed_kernel<G4A_WEIGHT_Q4K, 1>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 2>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 3>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 4>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 5>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 6>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 7>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 8>}};
+      e = g4a_launch(fixed[weight_format][S - 1], grid, dim3(kGemvThreads), smem, ctx->stream, true, input, J);
+    } else {
+      auto kern = weight_format == G4A_WEIGHT_F16 ? gemv_kernel<G4A_WEIGHT_F16>
+                  : weight_format == G4A_WEIGHT_Q8 ? gemv_kernel<G4A_WEIGHT_Q8>
+                                                   : gemv_kernel<G4A_WEIGHT_Q4K>;
+      if (smem > 48u * 1024u) {
+        const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (a != cudaSuccess) return g4a_cuda_fail(a, "cudaFuncSetAttribute(gemv)");
+      }
+      e = g4a_launch(kern, grid, dim3(kGemvThreads), smem, ctx->stream, true, input, N, J);
     }
-    e = g4a_launch(kern, grid, dim3(kGemvThreads), smem, ctx->stream, true, input, N, J);
   }
   if (e != cudaSuccess) return g4a_cuda_fail(e, "launch gemv");
   return G4A_OK;
