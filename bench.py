@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--ncu-prefill", type=int, default=-1, metavar="W",
                     help="small profiling workload: config[3] prefill with sliding window W (0 = causal), "
                          "three launches, no timing")
+    ap.add_argument("--ncu-matmul", type=int, default=-1, metavar="FMT",
+                    help="only run three lm-head sized GEMV launches (262144 x 1536) of weight format FMT "
+                         "(0 f16, 1 Q8, 2 4-bit), for an ncu capture")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the prefill, batched-paged and split-KV 1M measurements")
     ap.add_argument("--ncu-case", type=int, default=0, metavar="L",
@@ -834,10 +837,39 @@ def run_ncu_prefill(W: int) -> int:
     return 0
 
 
+def run_ncu_matmul(fmt: int) -> int:
+    """Three launches of one lm-head sized GEMV (weights 252 MB at 4 bits, above L2), for ncu."""
+    import torch
+
+    import g4attn
+
+    ctx = g4attn.Context(0)
+    M, N = 262144, 1536
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    n = M * N
+    if fmt == 0:
+        w, sc = (torch.randn(n, generator=g, device="cuda") * 0.05).half(), None
+    else:
+        per_word = 4 if fmt == 1 else 8
+        w = torch.randint(-2**31, 2**31 - 1, (n // per_word,), generator=g, device="cuda", dtype=torch.int32)
+        sc = (torch.rand(n // (32 if fmt == 1 else 16), generator=g, device="cuda") * 1e-3).half()
+    x = torch.randn(N, generator=g, device="cuda")
+    out = torch.empty(M, device="cuda")
+    for _ in range(3):
+        ctx.matmul(fmt, x, w, sc, out, M=M, N=N)
+    ctx.sync()
+    print(json.dumps({"ncu_matmul": fmt, "out_abs_sum": float(out.abs().sum())}))
+    ctx.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.ncu_prefill >= 0:
         return run_ncu_prefill(args.ncu_prefill)
+    if args.ncu_matmul >= 0:
+        return run_ncu_matmul(args.ncu_matmul)
     if args.ncu_case:
         return run_ncu_case(args.ncu_case)
     if args.impl == "reference":

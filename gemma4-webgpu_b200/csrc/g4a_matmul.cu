@@ -15,8 +15,8 @@
 // (Q8) or 4-byte (Q4K) load per lane per 256-element step brings the lane exactly its threads'
 // elements, and a warp load is one contiguous 512 / 256 / 128-byte run of the row.  The tree
 // levels 128 .. 8 pair thread t with t + stride = 8(l + stride/8) + e, i.e. lane l + stride/8
-// with the same e: five shuffle levels; levels 4, 2, 1 are lane-local in lane 0.  The result
-// is bit-identical to the shader's order.  The f16 path for N % 8 != 0 (or an unaligned
+// with the same e (done as a butterfly that halves the values per lane at each level).  The
+// result is bit-identical to the shader's order.  The f16 path for N % 8 != 0 (or an unaligned
 // weight) uses the other natural layout, threads t = l + 32e, with scalar 2-byte loads.
 //
 // Roofline: HBM-bound streaming of the weight (2 / 1.0625 / 0.625 bytes per element); the
@@ -174,17 +174,44 @@ __device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, 
   }
 }
 
-// The 256-thread tree for threads t = 8 lane + e; lane 0 returns p[0].
-__device__ __forceinline__ float tree_8l_e(float (&acc)[8]) {
+// The 256-thread tree for threads t = 8 lane + e, as a butterfly that halves the values each
+// lane holds at every level, so 12 shuffles do what 40 would in the direct form.  Each add
+// pairs exactly the shader's operands p[t] and p[t + stride]; only which lane computes it (and
+// so the operand order) changes, and IEEE addition is commutative.  Every lane returns p[0].
+//   stride 128: lanes L and L^16 (t = 8(L&15) + e): the lower lane keeps e 0-3, the upper 4-7;
+//               then lane L holds t = 8(L&15) + 4(L>>4) + e, e < 4.
+//   stride  64: lanes L and L^8: lower keeps e 0-1, upper 2-3 -> t = 8(L&7) + 4(L>>4) + 2((L>>3)&1) + e.
+//   stride  32: lanes L and L^4: lower keeps e 0, upper 1 -> one value, t = 8(L&3) + 4(L>>4) +
+//               2((L>>3)&1) + ((L>>2)&1).
+//   strides 16, 8, 4, 2, 1: partners at lane bits 1, 0, 4, 3, 2 (both lanes form the sum).
+__device__ __forceinline__ float tree_butterfly(const float (&a)[8], int lane) {
+  const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0, u4 = (lane & 4) != 0;
+  float b[4];
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1)  // strides 128, 64, 32, 16, 8
+  for (int e = 0; e < 4; e++) {
+    const float keep = u16 ? a[e + 4] : a[e];
+    const float send = u16 ? a[e] : a[e + 4];
+    b[e] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+  float c[2];
 #pragma unroll
-    for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], __shfl_down_sync(0xffffffffu, acc[e], off));
-#pragma unroll
-  for (int e = 0; e < 4; e++) acc[e] = __fadd_rn(acc[e], acc[e + 4]);  // stride 4
-  acc[0] = __fadd_rn(acc[0], acc[2]);                                   // stride 2
-  acc[1] = __fadd_rn(acc[1], acc[3]);
-  return __fadd_rn(acc[0], acc[1]);                                     // stride 1
+  for (int e = 0; e < 2; e++) {
+    const float keep = u8 ? b[e + 2] : b[e];
+    const float send = u8 ? b[e] : b[e + 2];
+    c[e] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  float d;
+  {
+    const float keep = u4 ? c[1] : c[0];
+    const float send = u4 ? c[0] : c[1];
+    d = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 2));   // stride 16
+  d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 1));   // stride 8
+  d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 16));  // stride 4
+  d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 8));   // stride 2
+  d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, 4));   // stride 1
+  return d;
 }
 
 // Stage input[0, N) into shared memory (after the PDL wait).
@@ -246,7 +273,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __re
       for (int u = 0; u < B; u++)
         if (j + u < mine) consume_step<FMT>(raw[u], j + u, lane, xs, acc);
     }
-    const float v = tree_8l_e(acc);
+    const float v = tree_butterfly(acc, lane);
     if (lane == 0) jb.out[m] = v;
   };
   if constexpr (kPipe) {
@@ -307,7 +334,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int u = 0; u < S; u++) consume_step<FMT>(raw[u], (uint32_t)u, lane, xs, acc);
-    const float v = tree_8l_e(acc);
+    const float v = tree_butterfly(acc, lane);
     uint32_t m;
     const GemvJob& jb = job_of(jobs, row, m);
     if (lane == 0) jb.out[m] = v;
