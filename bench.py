@@ -673,6 +673,32 @@ def run_prefill(ctx, torch):
         fl = synth.prefill_flops(T, W)
         res[name] = {"attn_us": us, "tflops": fl / (us * 1e-6) / 1e12, "frac_of_peak": fl / (us * 1e-6) / 1e12 / bf16,
                      "prep_plus_attn_us": us_both, "flops": fl}
+    # Gemma's global layers: head_dim 512 (warp-MMA kernel), same prompt length; 4 * NQH * 512
+    # flops per unmasked pair.
+    del q16, kc, vc, out
+    H5 = 512
+    k5 = torch.randn((T, NKH, H5), generator=g, device="cuda").half()
+    v5 = torch.randn((T, NKH, H5), generator=g, device="cuda").half()
+    q5 = (torch.randn((T, NQH, H5), generator=g, device="cuda") / 8).half()
+    o5 = torch.empty((T, NQH, H5), device="cuda")
+    for name, W in (("hd512_causal", 0), ("hd512_sliding_512", 512)):
+        def attn5():
+            ctx.prefill_attn(q5, k5, v5, o5, T=T, start_pos=0, num_q_heads=NQH, num_kv_heads=NKH, head_dim=H5,
+                             scale=1.0, sliding_window=W)
+
+        for _ in range(3):
+            attn5()
+        torch.cuda.synchronize()
+        n = 10
+        e0.record()
+        for _ in range(n):
+            attn5()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        fl = synth.prefill_flops(T, W, hd=H5)
+        res[name] = {"attn_us": us, "tflops": fl / (us * 1e-6) / 1e12, "frac_of_peak": fl / (us * 1e-6) / 1e12 / bf16,
+                     "flops": fl, "kernel": "prefill_wide_kernel (mma.sync m16n8k16)"}
     return res
 
 

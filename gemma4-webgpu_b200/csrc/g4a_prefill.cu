@@ -716,8 +716,12 @@ extern "C" g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const 
     return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: pointers must be 16-byte aligned");
   if ((uint64_t)start_pos + T > 0xffffffffull) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: start_pos + T overflows");
   if (T == 0) return G4A_OK;
-  // The tensor-core kernel covers GQA 8:1 at head_dim 128 and 256; every other shape (Gemma's
-  // head_dim 512 global layers among them) runs through the decode kernels.
+  // The tcgen05 kernel covers GQA 8:1 at head_dim 128 and 256, the warp-MMA kernel of
+  // g4a_prefill_wide.cu GQA 8:1 at head_dim 512 (Gemma's global layers); every other shape runs
+  // through the decode kernels.
+  if (num_q_heads == (uint32_t)kHeadsPerKv * num_kv_heads && head_dim == 512)
+    return prefill_wide(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
+                        sliding_window);
   if (num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads || (head_dim != 128 && head_dim != 256))
     return prefill_via_decode(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, head_dim,
                               scale, sliding_window);
