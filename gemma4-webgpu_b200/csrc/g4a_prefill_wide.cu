@@ -94,40 +94,49 @@ __global__ void __launch_bounds__(kWideThreads, 1) prefill_wide_kernel(const __g
   const uint32_t tile = p.ntiles - 1u - blockIdx.x / p.nkh;  // latest (heaviest) tiles first
   const uint32_t t0 = tile * kWideTok;
   const uint32_t nt = min((uint32_t)kWideTok, p.T - t0);
-  const uint64_t hi_max = (uint64_t)p.start_pos + t0 + nt;  // keys [.., hi_max) exist in the cache
-  const uint64_t first_hi = (uint64_t)p.start_pos + t0 + 1;
-  const uint64_t lo_min = (p.window && first_hi > p.window) ? first_hi - p.window : 0;
-  const uint32_t j0 = (uint32_t)(lo_min / kWideKeys), j1 = (uint32_t)((hi_max + kWideKeys - 1) / kWideKeys);
+  // Key positions fit in 32 bits: the host checks start_pos + T < 2^32.
+  const uint32_t hi_max = p.start_pos + t0 + nt;  // keys [.., hi_max) exist in the cache
+  const uint32_t hi_min = p.start_pos + t0 + 1;   // the tile's first token sees keys below this
+  const uint32_t lo_min = (p.window && hi_min > p.window) ? hi_min - p.window : 0u;
+  const uint32_t lo_max = (p.window && hi_max > p.window) ? hi_max - p.window : 0u;  // last token's window start
+  const uint32_t j0 = lo_min / kWideKeys, j1 = (uint32_t)(((uint64_t)hi_max + kWideKeys - 1) / kWideKeys);
   const size_t kv_stride = (size_t)p.nkh * kWideHD;  // elements between consecutive cache rows
+  // 256 threads: thread `tid` copies chunk c = tid % 64 of rows tid / 64 + 4 i.
+  const uint32_t cc = (uint32_t)tid & 63u, n0 = (uint32_t)tid >> 6;
 
   g4a::pdl_wait_primary();  // q16 and the cache rows are written by the preceding kernels
 
-  // Q tile: row r = token * 8 + head; 64 chunks per row, 16 per thread.
-  for (int i = tid; i < kWideRows * 64; i += kWideThreads) {
-    const uint32_t r = (uint32_t)i >> 6, c = (uint32_t)i & 63u;
-    const uint32_t tok = r >> 3, head = r & 7u;
+  // Q tile: row r = token * 8 + head (the 8 heads of a token are contiguous in q16).
+#pragma unroll
+  for (int i = 0; i < kWideRows / 4; i++) {
+    const uint32_t r = n0 + 4u * i, tok = r >> 3, head = r & 7u;
     const bool ok = tok < nt;
-    const __half* src = ok ? p.q16 + ((size_t)(t0 + tok) * p.nqh + kvh * 8u + head) * kWideHD + c * 8u : p.q16;
-    cp_async16(sbase + kOffQ + swz(r, c), src, ok);
+    const __half* src = ok ? p.q16 + ((size_t)(t0 + tok) * p.nqh + kvh * 8u + head) * kWideHD + cc * 8u : p.q16;
+    cp_async16(sbase + kOffQ + swz(r, cc), src, ok);
   }
+  const size_t lane_off = (size_t)kvh * kWideHD + cc * 8u;
   auto load_block = [&](uint32_t j, int buf) {
-    for (int i = tid; i < kWideKeys * 64; i += kWideThreads) {
-      const uint32_t n = (uint32_t)i >> 6, c = (uint32_t)i & 63u;
-      const uint64_t key = (uint64_t)j * kWideKeys + n;
-      const bool ok = key < hi_max;
-      const size_t off = ok ? (size_t)key * kv_stride + (size_t)kvh * kWideHD + c * 8u : 0;
-      cp_async16(sbase + kOffK + buf * (kWideKeys * kRowBytes) + swz(n, c), p.k + off, ok);
-      cp_async16(sbase + kOffV + buf * (kWideKeys * kRowBytes) + swz(n, c), p.v + off, ok);
+    const uint32_t kb = j * kWideKeys;
+    const size_t row0 = ((size_t)kb + n0) * kv_stride + lane_off;
+    const uint32_t dk = sbase + kOffK + buf * (kWideKeys * kRowBytes), dv = dk + (kOffV - kOffK);
+#pragma unroll
+    for (int i = 0; i < kWideKeys / 4; i++) {
+      const uint32_t n = n0 + 4u * i;
+      const bool ok = (uint64_t)kb + n < hi_max;
+      const size_t off = ok ? row0 + (size_t)(4 * i) * kv_stride : 0;
+      cp_async16(dk + swz(n, cc), p.k + off, ok);
+      cp_async16(dv + swz(n, cc), p.v + off, ok);
     }
   };
   load_block(j0, 0);
   cp_async_commit();  // group: Q + first block
 
   // Rows of this lane: A = (token 2g, head lane/4) in c0/c1, B = (token 2g+1, same head) in c2/c3.
+  // Rows past T are computed like the others (their q rows are zero) and never written.
   const uint32_t tokA = t0 + 2u * g, tokB = tokA + 1u;
-  const uint64_t hiA = (uint64_t)p.start_pos + tokA + 1, hiB = hiA + 1;
-  const uint64_t loA = (p.window && hiA > p.window) ? hiA - p.window : 0;
-  const uint64_t loB = (p.window && hiB > p.window) ? hiB - p.window : 0;
+  const uint32_t hiA = p.start_pos + tokA + 1, hiB = hiA + 1;
+  const uint32_t loA = (p.window && hiA > p.window) ? hiA - p.window : 0u;
+  const uint32_t loB = (p.window && hiB > p.window) ? hiB - p.window : 0u;
   const bool rowA = tokA < p.T, rowB = tokB < p.T;
 
   float o[32][4];
@@ -180,19 +189,32 @@ __global__ void __launch_bounds__(kWideThreads, 1) prefill_wide_kernel(const __g
 #pragma unroll
       for (int e = 0; e < 4; e++) s[t][e] = __fadd_rn(s[t][e], xpeer[(t * 4 + e) * 32]);
 
-    // ---- mask, running max, P
+    // ---- mask (only blocks that cross some row's window edge or diagonal), running max, P
     float bmA = -INFINITY, bmB = -INFINITY;
+    const uint32_t kb = j * kWideKeys;
+    if (kb >= lo_max && (uint64_t)kb + kWideKeys <= hi_min) {  // every key visible to every row of the tile
 #pragma unroll
-    for (int t = 0; t < 4; t++)
+      for (int t = 0; t < 4; t++)
 #pragma unroll
-      for (int e = 0; e < 2; e++) {
-        const uint64_t key = (uint64_t)j * kWideKeys + t * 8 + 2 * (lane & 3) + e;
-        const bool okA = rowA && key >= loA && key < hiA, okB = rowB && key >= loB && key < hiB;
-        s[t][e] = okA ? s[t][e] * p.scale_log2 : -INFINITY;
-        s[t][2 + e] = okB ? s[t][2 + e] * p.scale_log2 : -INFINITY;
-        bmA = fmaxf(bmA, s[t][e]);
-        bmB = fmaxf(bmB, s[t][2 + e]);
-      }
+        for (int e = 0; e < 2; e++) {
+          s[t][e] *= p.scale_log2;
+          s[t][2 + e] *= p.scale_log2;
+          bmA = fmaxf(bmA, s[t][e]);
+          bmB = fmaxf(bmB, s[t][2 + e]);
+        }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const uint32_t key = kb + (uint32_t)(t * 8 + 2 * (lane & 3) + e);
+          const bool okA = key >= loA && key < hiA, okB = key >= loB && key < hiB;
+          s[t][e] = okA ? s[t][e] * p.scale_log2 : -INFINITY;
+          s[t][2 + e] = okB ? s[t][2 + e] * p.scale_log2 : -INFINITY;
+          bmA = fmaxf(bmA, s[t][e]);
+          bmB = fmaxf(bmB, s[t][2 + e]);
+        }
+    }
 #pragma unroll
     for (int off = 1; off <= 2; off <<= 1) {
       bmA = fmaxf(bmA, __shfl_xor_sync(0xffffffffu, bmA, off));
