@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--ncu-prefill", type=int, default=-1, metavar="W",
                     help="small profiling workload: config[3] prefill with sliding window W (0 = causal), "
                          "three launches, no timing")
+    ap.add_argument("--ncu-head-dim", type=int, default=256, choices=[128, 256, 512],
+                    help="head_dim of the --ncu-prefill case (512: the warp-MMA kernel of the global layers)")
     ap.add_argument("--ncu-matmul", type=int, default=-1, metavar="FMT",
                     help="only run three lm-head sized GEMV launches (262144 x 1536) of weight format FMT "
                          "(0 f16, 1 Q8, 2 4-bit), for an ncu capture")
@@ -831,8 +833,8 @@ def run_ncu_case(L: int) -> int:
     return 0
 
 
-def run_ncu_prefill(W: int) -> int:
-    """Prep + three prefill-attention launches of config[3] (T = 4096), for ncu captures."""
+def run_ncu_prefill(W: int, HD: int = HD) -> int:
+    """Prep + three prefill-attention launches of config[3] (T = 4096) at head_dim HD, for ncu."""
     import numpy as np
     import torch
 
@@ -893,7 +895,7 @@ def run_ncu_matmul(fmt: int) -> int:
 def main():
     args = parse()
     if args.ncu_prefill >= 0:
-        return run_ncu_prefill(args.ncu_prefill)
+        return run_ncu_prefill(args.ncu_prefill, args.ncu_head_dim)
     if args.ncu_matmul >= 0:
         return run_ncu_matmul(args.ncu_matmul)
     if args.ncu_case:
