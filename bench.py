@@ -436,31 +436,39 @@ def run_ours(args):
 
 
 def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
-    """The reference-facing path: pinned host q/k/v in, g4a_attn_decode_layer (producers +
-    attention), host out back, for every layer call, through the raw C ABI.  Every rank runs its
-    own calls; the value is the whole job's bytes over the slowest rank's device time."""
+    """The reference-facing path: pinned host q | k | v in, the layer (producers + attention),
+    host output back, for every layer call, through the raw C ABI: one g4a_attn_decode_layer_io
+    call per layer call (it enqueues the copy in, the layer kernels and the copy out).  Every
+    rank runs its own calls; the value is the whole job's bytes over the slowest rank's device
+    time."""
+    import ctypes
+
     import numpy as np
 
-    from g4attn import _ptr
-    from g4attn._lib import call
+    from g4attn._lib import G4A_OK, G4AError, load
 
     dev = torch.device("cuda", ctx.device)
     rng = np.random.default_rng(100 + rank)
-    # q | k | v of a token in one pinned host buffer, copied with one call
+    # q | k | v of a token in one pinned host buffer
     hqkv = torch.from_numpy(rng.standard_normal((NQH + 2 * NKH) * HD).astype(np.float32)).pin_memory()
     hout = torch.zeros((NQH, HD), dtype=torch.float32).pin_memory()
     qkv = torch.empty_like(hqkv, device=dev)
-    q, k, v = qkv[:NQH * HD], qkv[NQH * HD:(NQH + NKH) * HD], qkv[(NQH + NKH) * HD:]
     out = torch.empty((NQH, HD), device=dev)
     w = torch.ones(HD, dtype=torch.float16, device=dev)
-    h = ctx.handle
     nb = lambda t: t.numel() * t.element_size()  # noqa: E731
+    lib = load()
+    fn = lib.g4a_attn_decode_layer_io
+    vp, u32, f32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_float
+    # argument tuples built once, so a layer call costs one foreign call
+    args = [(ctx.handle, vp(hqkv.data_ptr()), vp(qkv.data_ptr()), vp(out.data_ptr()), vp(hout.data_ptr()),
+             vp(w.data_ptr()), vp(w.data_ptr()), vp(None), vp(kcs[r].data_ptr()), vp(vcs[r].data_ptr()), u32(NQH),
+             u32(NKH), u32(HD), f32(EPS), u32(L - 1), u32(L - 1), u32(L), u32(L), f32(1e6), u32(0), f32(1.0),
+             u32(0), u32(1)) for r in range(R)]
 
     def layer_call(r):
-        call("g4a_memcpy_h2d", h, _ptr(qkv), _ptr(hqkv.data_ptr()), nb(hqkv))
-        call("g4a_attn_decode_layer", h, _ptr(q), _ptr(k), _ptr(v), _ptr(w), _ptr(w), _ptr(None), _ptr(kcs[r]),
-             _ptr(vcs[r]), _ptr(out), NQH, NKH, HD, EPS, L - 1, L - 1, L, L, 1e6, 0, 1.0, 0, 1)
-        call("g4a_memcpy_d2h", h, _ptr(hout.data_ptr()), _ptr(out), nb(out))
+        st = fn(*args[r])
+        if st != G4A_OK:
+            raise G4AError(st, "g4a_attn_decode_layer_io", (lib.g4a_last_error() or b"").decode())
 
     for i in range(min(R, 8)):
         layer_call(i % R)
@@ -478,8 +486,9 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
     return {"value": kv_bytes(L) * calls * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": nb(hqkv), "d2h_bytes_per_step": nb(hout),
             "us_per_layer": ms * 1e3 / calls, "layer_calls_per_rank": calls,
-            "path": "g4a_memcpy_h2d of q|k|v + g4a_attn_decode_layer (q/k norm+RoPE, v_norm, store, attention) + "
-                    "g4a_memcpy_d2h of the output, per layer call, pinned host buffers"}
+            "path": "one g4a_attn_decode_layer_io call per layer call: cudaMemcpyAsync of q|k|v from pinned host "
+                    "memory, the layer (q/k norm+RoPE, v_norm, store, attention), cudaMemcpyAsync of the output "
+                    "to pinned host memory"}
 
 
 def _max_over_ranks(torch, dist, value: float) -> float:

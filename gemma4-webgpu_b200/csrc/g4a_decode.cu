@@ -1440,3 +1440,91 @@ extern "C" g4a_status g4a_attn_decode_layer(g4a_ctx* ctx, float* q, float* k, fl
   return decode_contiguous(ctx, q, k_cache, v_cache, out, num_q_heads, num_kv_heads, head_dim, kv_len, scale,
                            sliding_window, true);
 }
+
+namespace {
+
+// Copies n4 float4 between device memory and pinned host memory mapped into the device's
+// address space, as a kernel on the context's stream instead of a copy-engine transfer (which
+// would break the programmatic-launch chain of the layer's kernels).  Host to device: the host
+// data does not depend on the preceding kernel, so it is loaded before the wait, and stored to
+// the device buffer (which the preceding call's kernels may still read) after it.  Device to
+// host: the wait comes first (the source is the preceding kernel's output).
+__global__ void __launch_bounds__(256) io_copy_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                                      uint32_t n4, int src_is_host) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (src_is_host) {
+    if (i < n4) v = src[i];
+    g4a::pdl_wait_primary();
+  } else {
+    g4a::pdl_wait_primary();
+    if (i < n4) v = __ldcg(src + i);
+  }
+  if (i < n4) dst[i] = v;
+  g4a::pdl_launch_dependents();
+}
+
+// The device address of `host` if it is pinned host memory the device can reach, else nullptr.
+void* mapped_host_address(const void* host) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+    (void)cudaGetLastError();  // clear the (non-sticky) error of the query
+    return nullptr;
+  }
+  return (a.type == cudaMemoryTypeHost && a.devicePointer) ? a.devicePointer : nullptr;
+}
+
+// dst <- src (bytes) on the context's stream: the copy kernel when the host side is mapped
+// pinned memory and both sides are 16-byte aligned, else cudaMemcpyAsync.
+g4a_status io_copy(g4a_ctx* ctx, void* dst, const void* src, size_t bytes, bool to_device) {
+  const void* host = to_device ? src : dst;
+  void* mapped = mapped_host_address(host);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | bytes) & 15u) == 0;
+  if (mapped && aligned && bytes / 16 <= 0xffffffffull) {
+    const uint32_t n4 = (uint32_t)(bytes / 16);
+    const void* s = to_device ? mapped : src;
+    void* d = to_device ? dst : mapped;
+    const cudaError_t e = g4a_launch(io_copy_kernel, dim3((n4 + 255) / 256), dim3(256), 0, ctx->stream, true,
+                                     reinterpret_cast<const float4*>(s), reinterpret_cast<float4*>(d), n4,
+                                     to_device ? 1 : 0);
+    if (e != cudaSuccess) return g4a_cuda_fail(e, "launch io_copy_kernel");
+    return G4A_OK;
+  }
+  G4A_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost,
+                               ctx->stream));
+  return G4A_OK;
+}
+
+}  // namespace
+
+extern "C" g4a_status g4a_attn_decode_layer_io(g4a_ctx* ctx, const float* qkv_host, float* qkv_dev, float* out_dev,
+                                               float* out_host, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                               const uint16_t* rope_freqs, uint16_t* k_cache, uint16_t* v_cache,
+                                               uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim,
+                                               float eps, uint32_t position, uint32_t slot, uint32_t kv_len,
+                                               uint32_t max_seq_len, float theta, uint32_t apply_divisor,
+                                               float scale, uint32_t sliding_window, uint32_t is_producer) {
+  G4A_CHECK_CTX(ctx);
+  if (!qkv_host || !qkv_dev || !out_dev || !out_host)
+    return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer_io: null host or device buffer");
+  const size_t q_elems = (size_t)num_q_heads * head_dim, kv_elems = (size_t)num_kv_heads * head_dim;
+  const size_t in_elems = q_elems + (is_producer ? 2 * kv_elems : 0);
+  float* q = qkv_dev;
+  float* k = qkv_dev + q_elems;
+  float* v = k + kv_elems;
+  // Validate before anything is enqueued, so a rejected call leaves the stream untouched.
+  if (g4a_status s = check_common(__func__, q, k_cache, v_cache, out_dev, num_q_heads, num_kv_heads, head_dim))
+    return s;
+  if (!q_norm_w || (is_producer && !k_norm_w)) return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer_io: null norm weight");
+  if (apply_divisor && !rope_freqs)
+    return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer_io: apply_divisor without rope_freqs");
+  if ((is_producer && slot >= max_seq_len) || kv_len > max_seq_len)
+    return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer_io: slot %u / kv_len %u vs max_seq_len %u", slot, kv_len,
+                    max_seq_len);
+  if (g4a_status s = io_copy(ctx, qkv_dev, qkv_host, in_elems * sizeof(float), true)) return s;
+  if (g4a_status s = g4a_attn_decode_layer(ctx, q, k, v, q_norm_w, k_norm_w, rope_freqs, k_cache, v_cache, out_dev,
+                                           num_q_heads, num_kv_heads, head_dim, eps, position, slot, kv_len,
+                                           max_seq_len, theta, apply_divisor, scale, sliding_window, is_producer))
+    return s;
+  return io_copy(ctx, out_host, out_dev, q_elems * sizeof(float), false);
+}

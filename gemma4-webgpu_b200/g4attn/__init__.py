@@ -232,6 +232,17 @@ class Context:
              float(eps), int(position), int(slot), int(kv_len), int(max_seq_len), float(theta),
              int(apply_divisor), float(scale), int(sliding_window), int(is_producer))
 
+    def attn_decode_layer_io(self, qkv_host, qkv_dev, out_dev, out_host, q_norm_w, k_norm_w, rope_freqs, k_cache,
+                             v_cache, *, num_q_heads, num_kv_heads, head_dim, eps, position, slot, kv_len,
+                             max_seq_len, theta, apply_divisor=0, scale=1.0, sliding_window=0, is_producer=1) -> None:
+        """attn_decode_layer with the token's packed q | k | v and the output in (pinned) host
+        memory: one call enqueues the copy in, the layer and the copy out."""
+        call("g4a_attn_decode_layer_io", self._h, _ptr(qkv_host.data_ptr()), _ptr(qkv_dev), _ptr(out_dev),
+             _ptr(out_host.data_ptr()), _ptr(q_norm_w), _ptr(k_norm_w), _ptr(rope_freqs), _ptr(k_cache),
+             _ptr(v_cache), num_q_heads, num_kv_heads, head_dim, float(eps), int(position), int(slot), int(kv_len),
+             int(max_seq_len), float(theta), int(apply_divisor), float(scale), int(sliding_window),
+             int(is_producer))
+
     # ---------------------------------------------------------------- memory and IPC
     def alloc(self, nbytes: int) -> int:
         """Device allocation through the library (cudaMalloc); returns the address."""

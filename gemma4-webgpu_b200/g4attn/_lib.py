@@ -74,6 +74,8 @@ SIGNATURES: dict[str, list] = {
     "g4a_lse_merge": [_p, _p, _u32, _u32, _u32, _p],
     "g4a_attn_decode_layer": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _f, _u32, _u32, _u32,
                               _u32, _f, _u32, _f, _u32, _u32],
+    "g4a_attn_decode_layer_io": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _f, _u32, _u32, _u32,
+                                 _u32, _f, _u32, _f, _u32, _u32],
     "g4a_prefill_qkv_prep": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _f,
                              _u32],
     "g4a_prefill_attn": [_p, _p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _f, _u32],

@@ -212,6 +212,25 @@ g4a_status g4a_attn_decode_layer(g4a_ctx* ctx, float* q, float* k, float* v,
                                  uint32_t max_seq_len, float theta, uint32_t apply_divisor,
                                  float scale, uint32_t sliding_window, uint32_t is_producer);
 
+/* g4a_attn_decode_layer with its token's inputs and its output in host memory, for a caller
+ * whose q / k / v come from the host (no counterpart in the reference, where they are produced
+ * on the GPU): in one call, copies q | k | v (packed f32: num_q_heads*head_dim, then
+ * num_kv_heads*head_dim twice; only q for a consumer layer) from qkv_host to the device work
+ * buffer qkv_dev, runs the layer on it (q, k and v are then modified in place in qkv_dev), and
+ * copies the output [num_q_heads, head_dim] from out_dev back to out_host.  Everything is
+ * enqueued on the context's stream; out_host holds the result after g4a_sync, and qkv_host must
+ * keep its contents until then.  With pinned (page-locked) host buffers and 16-byte aligned
+ * pointers the two copies are small kernels that reach the host memory directly, chained to the
+ * layer's kernels; otherwise they are ordinary asynchronous copies (synchronous for pageable
+ * memory). */
+g4a_status g4a_attn_decode_layer_io(g4a_ctx* ctx, const float* qkv_host, float* qkv_dev, float* out_dev,
+                                    float* out_host, const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                    const uint16_t* rope_freqs, uint16_t* k_cache, uint16_t* v_cache,
+                                    uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim, float eps,
+                                    uint32_t position, uint32_t slot, uint32_t kv_len, uint32_t max_seq_len,
+                                    float theta, uint32_t apply_divisor, float scale, uint32_t sliding_window,
+                                    uint32_t is_producer);
+
 /* ------------------------------------------------------------------ prefill */
 
 /* Prefill input stage for T tokens at positions start_pos..start_pos+T-1 (the reference runs

@@ -68,3 +68,46 @@ def test_consumer_layer_reads_shared_cache(ctx, oracle):
     ref = oracle.decode_attn_f64(qn, before, host(vc), num_q_heads=8, num_kv_heads=1, head_dim=hd, kv_len=L,
                                  sliding_window=512)
     assert_attention_close(host(out), ref, what="consumer layer")
+
+
+@pytest.mark.parametrize("layer,producer,pinned", [(0, 1, True), (4, 1, True), (5, 0, True), (0, 1, False)])
+def test_layer_io_entry_matches_device_path(ctx, layer, producer, pinned):
+    """g4a_attn_decode_layer_io (host q | k | v in, host output back, one call) gives the same bits
+    as the copy-in, g4a_attn_decode_layer, copy-out sequence, for the caches too; a consumer
+    layer copies only q and leaves the shared cache alone.  Pinned host buffers take the copy
+    kernels, pageable ones the ordinary copies."""
+    cfg = GemmaAttnConfig()
+    hd, theta, W, div = cfg.head_dim(layer), cfg.rope_theta(layer), cfg.window(layer), cfg.apply_divisor(layer)
+    rf = gemma_rope_freqs(512, 64) if div else None
+    L = 700
+    raw = synth.raw_layer(L + layer, L, hd=hd, theta=theta)
+    f16 = lambda a: dev(a.view(np.uint16)).view(torch.float16)  # noqa: E731
+    kc0, vc0 = gpu_build_cache(ctx, raw.k[: L - 1], raw.v[: L - 1], raw.k_w, theta=theta, apply_divisor=div,
+                               rope_freqs=rf, max_seq=L + 4)
+    pos = L - 1
+    kw = dict(num_q_heads=8, num_kv_heads=1, head_dim=hd, eps=EPS, position=pos, slot=pos, kv_len=L,
+              max_seq_len=L + 4, theta=theta, apply_divisor=div, scale=1.0, sliding_window=W, is_producer=producer)
+    qkv = np.concatenate([raw.q[0].reshape(-1), raw.k[pos].reshape(-1), raw.v[pos].reshape(-1)]).astype(np.float32)
+    # device path
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    qd, kd, vd = dev(raw.q[0]), dev(raw.k[pos]), dev(raw.v[pos])
+    out1 = torch.zeros((8, hd), device="cuda")
+    ctx.attn_decode_layer(qd, kd, vd, f16(raw.q_w), f16(raw.k_w), f16(rf) if rf is not None else None, kc1, vc1,
+                          out1, **kw)
+    # host-buffer entry, twice in a row into the same pinned output
+    kc2, vc2 = kc0.clone(), vc0.clone()
+    hin = torch.from_numpy(qkv)
+    hout = torch.full((8, hd), float("nan"))
+    if pinned:
+        hin, hout = hin.pin_memory(), hout.pin_memory()
+    qkv_dev = torch.empty(qkv.size, device="cuda")
+    out_dev = torch.empty((8, hd), device="cuda")
+    for _ in range(2):
+        ctx.attn_decode_layer_io(hin, qkv_dev, out_dev, hout, f16(raw.q_w), f16(raw.k_w),
+                                 f16(rf) if rf is not None else None, kc2, vc2, **kw)
+    ctx.sync()
+    assert same_bits(hout.numpy(), host(out1))
+    assert same_bits(host(qkv_dev[: 8 * hd]), host(qd).reshape(-1))
+    assert same_bits(host(kc2), host(kc1)) and same_bits(host(vc2), host(vc1))
+    if not producer:
+        assert same_bits(host(kc2), host(kc0))
