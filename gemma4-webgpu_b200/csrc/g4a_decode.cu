@@ -1411,7 +1411,8 @@ g4a_status g4a_decode_attn_noalloc(g4a_ctx* ctx, const float* q, const uint16_t*
 }  // extern "C"
 
 // Producer stage launcher lives in g4a_producers.cu.
-g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, float* q, float* k, float* v, const uint16_t* qw, const uint16_t* kw,
+g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, const float* sq, const float* sk, const float* sv, float* q,
+                                  float* k, float* v, const uint16_t* qw, const uint16_t* kw,
                                   const uint16_t* rope_freqs, uint16_t* k_cache, uint16_t* v_cache, uint32_t nqh,
                                   uint32_t nkh, uint32_t hd, float eps, uint32_t position, uint32_t slot, float theta,
                                   uint32_t apply_div, bool is_producer);
@@ -1433,7 +1434,8 @@ extern "C" g4a_status g4a_attn_decode_layer(g4a_ctx* ctx, float* q, float* k, fl
     return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer: slot %u >= max_seq_len %u", slot, max_seq_len);
   if (kv_len > max_seq_len)
     return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer: kv_len %u > max_seq_len %u", kv_len, max_seq_len);
-  if (g4a_status s = g4a_launch_decode_prep(ctx, q, k, v, q_norm_w, k_norm_w, rope_freqs, k_cache, v_cache,
+  if (g4a_status s = g4a_launch_decode_prep(ctx, nullptr, nullptr, nullptr, q, k, v, q_norm_w, k_norm_w, rope_freqs,
+                                            k_cache, v_cache,
                                             num_q_heads, num_kv_heads, head_dim, eps, position, slot, theta,
                                             apply_divisor, is_producer != 0))
     return s;
@@ -1475,7 +1477,8 @@ void* mapped_host_address(const void* host) {
 }
 
 // dst <- src (bytes) on the context's stream: the copy kernel when the host side is mapped
-// pinned memory and both sides are 16-byte aligned, else cudaMemcpyAsync.
+// pinned memory and both sides are 16-byte aligned, else cudaMemcpyAsync.  (Used by
+// g4a_attn_decode_layer_io when only one of its host buffers is mapped.)
 g4a_status io_copy(g4a_ctx* ctx, void* dst, const void* src, size_t bytes, bool to_device) {
   const void* host = to_device ? src : dst;
   void* mapped = mapped_host_address(host);
@@ -1521,6 +1524,20 @@ extern "C" g4a_status g4a_attn_decode_layer_io(g4a_ctx* ctx, const float* qkv_ho
   if ((is_producer && slot >= max_seq_len) || kv_len > max_seq_len)
     return g4a_fail(G4A_EINVAL, "g4a_attn_decode_layer_io: slot %u / kv_len %u vs max_seq_len %u", slot, kv_len,
                     max_seq_len);
+  // Mapped pinned host buffers: the producer kernel reads the inputs straight from host memory
+  // (before its programmatic-launch wait) and the attention writes its output straight into
+  // host memory, so the call is the layer's own launches and nothing else.
+  void* in_map = mapped_host_address(qkv_host);
+  void* out_map = in_map ? mapped_host_address(out_host) : nullptr;
+  if (in_map && out_map && ((reinterpret_cast<uintptr_t>(in_map) | reinterpret_cast<uintptr_t>(out_map)) & 15u) == 0) {
+    const float* sq = static_cast<const float*>(in_map);
+    if (g4a_status s = g4a_launch_decode_prep(ctx, sq, sq + q_elems, sq + q_elems + kv_elems, q, k, v, q_norm_w,
+                                              k_norm_w, rope_freqs, k_cache, v_cache, num_q_heads, num_kv_heads,
+                                              head_dim, eps, position, slot, theta, apply_divisor, is_producer != 0))
+      return s;
+    return decode_contiguous(ctx, q, k_cache, v_cache, static_cast<float*>(out_map), num_q_heads, num_kv_heads,
+                             head_dim, kv_len, scale, sliding_window, true);
+  }
   if (g4a_status s = io_copy(ctx, qkv_dev, qkv_host, in_elems * sizeof(float), true)) return s;
   if (g4a_status s = g4a_attn_decode_layer(ctx, q, k, v, q_norm_w, k_norm_w, rope_freqs, k_cache, v_cache, out_dev,
                                            num_q_heads, num_kv_heads, head_dim, eps, position, slot, kv_len,

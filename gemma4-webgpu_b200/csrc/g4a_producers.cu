@@ -155,26 +155,67 @@ __global__ void __launch_bounds__(kWG) kv_store_kernel(const float* k, float* v,
 }
 
 // Whole decode-producer stage of one layer in a single launch: CTAs [0, nqh) norm+RoPE the q
-// heads in place; CTAs [nqh, nqh+nkh) (producer layers only) norm+RoPE the k head, v_norm the
-// v head, and write both as f16 to cache row `slot`.
-__global__ void __launch_bounds__(kWG) decode_prep_kernel(float* q, float* k, float* v, const __half* qw,
+// heads; CTAs [nqh, nqh+nkh) (producer layers only) norm+RoPE the k head, v_norm the v head,
+// and write both as f16 to cache row `slot`.  Results go to q / k / v (in place, the
+// reference's work buffers).  With sq != nullptr the inputs are read from sq / sk / sv instead
+// (e.g. mapped host memory that nothing on the device writes): those loads are issued before
+// the programmatic-launch wait, so their latency overlaps the preceding kernel.
+__global__ void __launch_bounds__(kWG) decode_prep_kernel(const float* sq, const float* sk, const float* sv,
+                                                           float* q, float* k, float* v, const __half* qw,
                                                            const __half* kw, const __half* rope_freqs,
                                                            __half* k_cache, __half* v_cache, int nqh, int nkh,
                                                            int hd, float eps, uint32_t position, uint32_t slot,
                                                            const __grid_constant__ RopePow tab, uint32_t apply_div) {
   __shared__ float xs[kMaxHeadDim];
   __shared__ float red[kWG];
+  __shared__ float xin[kMaxHeadDim];  // staged input of a separate-source call
+  constexpr int kPer = kMaxHeadDim / kWG;
   const int b = blockIdx.x;
+  const bool staged = sq != nullptr;
+  float p0[kPer], p1[kPer];
+  if (staged) {
+    const float* s0 = (b < nqh) ? sq + (size_t)b * hd : sk + (size_t)(b - nqh) * hd;
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+      const int i = threadIdx.x + u * kWG;
+      p0[u] = i < hd ? s0[i] : 0.f;
+    }
+    if (b >= nqh) {
+      const float* s1 = sv + (size_t)(b - nqh) * hd;
+#pragma unroll
+      for (int u = 0; u < kPer; u++) {
+        const int i = threadIdx.x + u * kWG;
+        p1[u] = i < hd ? s1[i] : 0.f;
+      }
+    }
+  }
+  // Launched as a programmatic dependent of the preceding kernel: everything it writes (q / k /
+  // v, the cache rows a previous attention may still read) and every in-place input waits for
+  // that kernel to finish; only the launch and the separate-source loads overlap it.
+  g4a::pdl_wait_primary();
+  auto stage = [&](const float (&pv)[kPer]) {
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+      const int i = threadIdx.x + u * kWG;
+      if (i < hd) xin[i] = pv[u];
+    }
+    __syncthreads();
+  };
   if (b < nqh) {
     float* qh = q + (size_t)b * hd;
-    norm_rope_head(qh, qh, nullptr, qw, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
+    if (staged) stage(p0);
+    norm_rope_head(staged ? xin : qh, qh, nullptr, qw, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
   } else {
     const int j = b - nqh;
     const size_t row = ((size_t)slot * nkh + j) * hd;
     float* kh = k + (size_t)j * hd;
-    norm_rope_head(kh, kh, k_cache + row, kw, rope_freqs, hd, eps, position, tab, apply_div, xs, red);
+    if (staged) stage(p0);
+    norm_rope_head(staged ? xin : kh, kh, k_cache + row, kw, rope_freqs, hd, eps, position, tab, apply_div, xs,
+                   red);
     float* vh = v + (size_t)j * hd;
-    vnorm_head(vh, vh, v_cache + row, hd, eps, true, xs, red);
+    // (norm_rope_head copied xin into xs behind a CTA barrier, so xin can take the v head)
+    if (staged) stage(p1);
+    vnorm_head(staged ? xin : vh, vh, v_cache + row, hd, eps, true, xs, red);
   }
   // Let a programmatically-dependent attention launch start its prologue.
   g4a::pdl_launch_dependents();
@@ -365,7 +406,8 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
 }  // extern "C"
 
 // Internal entry used by g4a_attn_decode_layer (g4a_decode.cu).
-g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, float* q, float* k, float* v, const uint16_t* qw,
+g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, const float* sq, const float* sk, const float* sv, float* q,
+                                  float* k, float* v, const uint16_t* qw,
                                   const uint16_t* kw, const uint16_t* rope_freqs, uint16_t* k_cache,
                                   uint16_t* v_cache, uint32_t nqh, uint32_t nkh, uint32_t hd, float eps,
                                   uint32_t position, uint32_t slot, float theta, uint32_t apply_div,
@@ -374,9 +416,11 @@ g4a_status g4a_launch_decode_prep(g4a_ctx* ctx, float* q, float* k, float* v, co
   uint32_t blocks = nqh + (is_producer ? nkh : 0u);
   if (blocks == 0) return G4A_OK;
   g4a_prof_scope ps(ctx, G4A_PROF_DECODE_PREP);
-  decode_prep_kernel<<<blocks, kWG, 0, ctx->stream>>>(q, k, v, (const __half*)qw, (const __half*)kw,
-                                                      (const __half*)rope_freqs, (__half*)k_cache,
-                                                      (__half*)v_cache, (int)nqh, (int)nkh, (int)hd, eps, position,
-                                                      slot, make_rope_pow(theta, hd), apply_div);
-  return g4a_check_launch("decode_prep_kernel");
+  const cudaError_t e = g4a_launch(decode_prep_kernel, dim3(blocks), dim3(kWG), 0, ctx->stream, true, sq, sk, sv,
+                                   q, k, v,
+                                   (const __half*)qw, (const __half*)kw, (const __half*)rope_freqs, (__half*)k_cache,
+                                   (__half*)v_cache, (int)nqh, (int)nkh, (int)hd, eps, position, slot,
+                                   make_rope_pow(theta, hd), apply_div);
+  if (e != cudaSuccess) return g4a_cuda_fail(e, "launch decode_prep_kernel");
+  return G4A_OK;
 }

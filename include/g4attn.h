@@ -219,9 +219,10 @@ g4a_status g4a_attn_decode_layer(g4a_ctx* ctx, float* q, float* k, float* v,
  * buffer qkv_dev, runs the layer on it (q, k and v are then modified in place in qkv_dev), and
  * copies the output [num_q_heads, head_dim] from out_dev back to out_host.  Everything is
  * enqueued on the context's stream; out_host holds the result after g4a_sync, and qkv_host must
- * keep its contents until then.  With pinned (page-locked) host buffers and 16-byte aligned
- * pointers the two copies are small kernels that reach the host memory directly, chained to the
- * layer's kernels; otherwise they are ordinary asynchronous copies (synchronous for pageable
+ * keep its contents until then.  When both host buffers are pinned (page-locked) memory the
+ * device can address, 16-byte aligned, there are no copies: the producer kernel reads q | k | v
+ * from host memory and the attention writes the output into host memory (out_dev is then not
+ * used).  Otherwise the two copies are ordinary asynchronous copies (synchronous for pageable
  * memory). */
 g4a_status g4a_attn_decode_layer_io(g4a_ctx* ctx, const float* qkv_host, float* qkv_dev, float* out_dev,
                                     float* out_host, const uint16_t* q_norm_w, const uint16_t* k_norm_w,

@@ -70,12 +70,13 @@ def test_consumer_layer_reads_shared_cache(ctx, oracle):
     assert_attention_close(host(out), ref, what="consumer layer")
 
 
-@pytest.mark.parametrize("layer,producer,pinned", [(0, 1, True), (4, 1, True), (5, 0, True), (0, 1, False)])
+@pytest.mark.parametrize("layer,producer,pinned", [(0, 1, True), (4, 1, True), (5, 0, True), (0, 1, False),
+                                                   (4, 1, "in")])
 def test_layer_io_entry_matches_device_path(ctx, layer, producer, pinned):
     """g4a_attn_decode_layer_io (host q | k | v in, host output back, one call) gives the same bits
     as the copy-in, g4a_attn_decode_layer, copy-out sequence, for the caches too; a consumer
-    layer copies only q and leaves the shared cache alone.  Pinned host buffers take the copy
-    kernels, pageable ones the ordinary copies."""
+    layer copies only q and leaves the shared cache alone.  With both host buffers pinned the
+    kernels read and write host memory directly; otherwise the call copies."""
     cfg = GemmaAttnConfig()
     hd, theta, W, div = cfg.head_dim(layer), cfg.rope_theta(layer), cfg.window(layer), cfg.apply_divisor(layer)
     rf = gemma_rope_freqs(512, 64) if div else None
@@ -98,8 +99,10 @@ def test_layer_io_entry_matches_device_path(ctx, layer, producer, pinned):
     kc2, vc2 = kc0.clone(), vc0.clone()
     hin = torch.from_numpy(qkv)
     hout = torch.full((8, hd), float("nan"))
-    if pinned:
-        hin, hout = hin.pin_memory(), hout.pin_memory()
+    if pinned is True:
+        hin, hout = hin.pin_memory(), hout.pin_memory()  # no copies: kernels reach host memory
+    elif pinned == "in":
+        hin = hin.pin_memory()  # a mapped input with a pageable output: the copy path
     qkv_dev = torch.empty(qkv.size, device="cuda")
     out_dev = torch.empty((8, hd), device="cuda")
     for _ in range(2):
