@@ -15,8 +15,8 @@ over ranks (each rank runs its own independent sequences: weak scaling, no colle
 
 Besides `value` the line carries: `roofline` (the split-KV kernel's achieved GB/s from live
 CUDA events vs the measured HBM copy peak, DRAM traffic from the committed ncu summary),
-`e2e` (same metric through the C ABI with pinned host buffers copied in and out every layer
-call), `cpu_baseline` (the CPU restatement of the reference chain on the host cores), `clocks`
+`e2e` (same metric through the C ABI, every layer call taking its q | k | v from pinned host
+memory and returning its output to pinned host memory), `cpu_baseline` (the CPU restatement of the reference chain on the host cores), `clocks`
 (nvidia-smi samples during the timed region) and `sweep` (4k / 128k contexts, N=1).
 """
 from __future__ import annotations
@@ -486,9 +486,9 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
     return {"value": kv_bytes(L) * calls * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": nb(hqkv), "d2h_bytes_per_step": nb(hout),
             "us_per_layer": ms * 1e3 / calls, "layer_calls_per_rank": calls,
-            "path": "one g4a_attn_decode_layer_io call per layer call: cudaMemcpyAsync of q|k|v from pinned host "
-                    "memory, the layer (q/k norm+RoPE, v_norm, store, attention), cudaMemcpyAsync of the output "
-                    "to pinned host memory"}
+            "path": "one g4a_attn_decode_layer_io call per layer call: the producer kernel reads q|k|v "
+                    "(10,240 B) from pinned host memory over PCIe, the layer runs (q/k norm+RoPE, v_norm, store, "
+                    "attention), the attention writes the output (8,192 B) into pinned host memory"}
 
 
 def _max_over_ranks(torch, dist, value: float) -> float:
