@@ -71,3 +71,27 @@ def test_create_without_gpu_fails_cleanly():
     st = _lib.load().g4a_create(0, ctypes.byref(h))
     assert st != 0 and not h.value
     assert _lib.load().g4a_last_error()
+
+
+def test_every_context_entry_rejects_a_null_context():
+    """Every entry point that takes a context checks it before anything else: with a null context
+    (and null / zero for the rest) it returns G4A_EINVAL with a message and touches no device."""
+    lib = _lib.load()
+    skip = {"g4a_create", "g4a_destroy"}  # create takes no context; destroy(NULL) is a no-op
+    checked = 0
+    for name, argtypes in _lib.SIGNATURES.items():
+        if name in skip:
+            continue
+        args = []
+        for t in argtypes:
+            if t in (ctypes.c_float, ctypes.c_double):
+                args.append(t(0.0))
+            elif t in (ctypes.c_uint32, ctypes.c_int, ctypes.c_size_t):
+                args.append(t(0))
+            else:
+                args.append(None)
+        st = getattr(lib, name)(*args)
+        assert st == 1, (name, st)
+        assert b"null context" in lib.g4a_last_error(), name
+        checked += 1
+    assert checked >= 25
