@@ -15,7 +15,9 @@ from pathlib import Path
 
 import numpy as np
 
-ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_golden.py /path/to/reference")
+ref = Path(sys.argv[1])
 d = np.load(ref / "public/ref/layer_0_detail.npz")
 out = Path(__file__).resolve().parent / "vnorm_layer0.npz"
 np.savez_compressed(
