@@ -13,8 +13,9 @@ over ranks (each rank runs its own independent sequences: weak scaling, no colle
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Besides `value` the line carries: `roofline` (the split-KV kernel's achieved GB/s from live
-CUDA events vs the measured HBM copy peak, DRAM traffic from the committed ncu summary),
+Besides `value` the line carries: `roofline` (one layer-call -- the split-KV kernel and its merge
+kernel -- timed in the graph vs the measured HBM copy peak, DRAM traffic per launch from a prior
+ncu capture),
 `e2e` (same metric through the C ABI, every layer call taking its q | k | v from pinned host
 memory and returning its output to pinned host memory), `cpu_baseline` (the CPU restatement of the reference chain on the host cores), `clocks`
 (nvidia-smi samples during the timed region) and `sweep` (4k / 128k contexts, N=1).
@@ -29,7 +30,6 @@ import io
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -84,13 +84,19 @@ def kv_bytes(L: int, window: int = 0) -> int:
     return 2 * vis * NKH * HD * 2 + 2 * NQH * HD * 4
 
 
-def ncu_traffic(kernel_file: str):
-    """DRAM bytes per launch recorded in the committed ncu summary, or None."""
-    f = ROOT / "profiles" / kernel_file
-    if not f.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch\s*[=:]\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of decode_splitkv_kernel<256>
+# from an ncu capture of `python bench.py --ncu-case 32768` (cold L2 before each replay), keyed by
+# kv_len.  A prior capture, not a measurement of this run.
+DECODE_NCU_TRAFFIC = {32768: 33624832}
+
+
+def workload_config(L: int, world: int) -> dict:
+    """The `config` object of both arms' JSON lines (the same workload: config[1] at kv_len L)."""
+    return {"workload": f"config[1] global decode: 8 q heads / 1 kv head, head_dim 256, f16 KV cache, "
+                        f"kv_len {L}, theta 1e6, scale 1.0, f32 out",
+            "kv_len": L, "kv_dtype": "f16", "global_batch": world, "seq_len": L,
+            "parallelism": f"replicas{world}: independent sequences per GPU, no collective",
+            "l2": "inputs larger than L2 (GPU arm: distinct layer caches rotated every step)"}
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -273,8 +279,8 @@ def run_reference(args):
     line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"config[1] global decode, 8q/1kv heads, head_dim 256, kv_len {L}",
-                       "kv_len_per_step": n},
+            "config": workload_config(L, args.gpus),
+            "sample": {"kv_len_per_step": n, "cores": nthreads},
             "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": nthreads, "kind": "port",
                              "sample": f"reference chain attn_score->softmax->attn_output (WGSL order, f32 caches) "
                                        f"over {n} of {L} keys per step, OpenMP {nthreads} threads"},
@@ -381,7 +387,6 @@ def run_ours(args):
     m_ms, m_n = ctx.profile_read("decode_merge")
     ctx.profile_enable(False)
     k_avg_us = k_ms / max(k_n, 1) * 1e3
-    achieved = per_layer / (k_avg_us * 1e-6) / 1e9
     launches_per_layer = (1 if k_n else 0) + (1 if m_n else 0)
 
     # ---- end to end through the C ABI with pinned host buffers
@@ -391,22 +396,26 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "us_per_layer": us_per_layer,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"config[1] global decode: 8 q heads / 1 kv head, head_dim 256, f16 KV cache, "
-                               f"kv_len {L}, theta 1e6, scale 1.0, f32 out",
-                   "kv_len": L, "layers_per_step": R, "kv_dtype": "f16",
-                   "l2": f"inputs larger than L2: {R} distinct layer caches ({R * per_layer / 2**20:.0f} MiB) "
-                         f"rotated every step",
-                   "global_batch": world, "seq_len": L,
-                   "parallelism": f"replicas{world}: independent sequences per GPU, no collective",
-                   "timing": "CUDA graph of one step replayed K times, CUDA events, max over ranks"},
+        "config": workload_config(L, world),
+        "setup": {"layers_per_step": R,
+                  "l2": f"inputs larger than L2: {R} distinct layer caches ({R * per_layer / 2**20:.0f} MiB) "
+                        f"rotated every step",
+                  "timing": "CUDA graph of one step replayed K times, CUDA events, max over ranks"},
         "hbm_frac_of_measured": value / world / hbm,
         "hbm_frac_of_nominal_8tbs": value / world / 8000.0,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "kernel": "decode_splitkv_kernel<256>",
-                     "kernel_us": k_avg_us, "merge_us": m_ms / max(m_n, 1) * 1e3,
-                     "algorithmic_bytes_per_launch": per_layer,
-                     "traffic": ncu_traffic("decode_splitkv_hd256_L32768.md") if L == 32768 else None,
-                     "step_frac": value / world / hbm},
+        # The dominant work is one layer-call: decode_splitkv_kernel<256> and merge_segments_kernel,
+        # PDL-chained, so the per-call time of the timed graph is the duration used (16 calls per
+        # step: R x us_per_launch = ms_per_step).
+        "roofline": {"bound": "hbm", "achieved": per_layer / (us_per_layer * 1e-6) / 1e9, "peak": hbm,
+                     "unit": "GB/s", "frac": per_layer / (us_per_layer * 1e-6) / 1e9 / hbm,
+                     "peak_kind": peak_kind,
+                     "kernel": "decode_splitkv_kernel<256> + merge_segments_kernel (one layer-call)",
+                     "us_per_launch": us_per_layer, "algorithmic_bytes_per_launch": per_layer,
+                     "traffic": DECODE_NCU_TRAFFIC.get(L),
+                     "traffic_source": "prior ncu capture of decode_splitkv_kernel<256> (bench.py --ncu-case 32768)"},
+        "profiler": {"decode_us": k_avg_us, "merge_us": m_ms / max(m_n, 1) * 1e3,
+                     "note": "per-launch CUDA events of an eager PDL-chained pass; each interval includes the "
+                             "launch's wait for its predecessor, so they overlap"},
         "gpu_launches": launches_per_layer * R * args.steps,
         "clocks": clocks,
         "e2e": e2e,

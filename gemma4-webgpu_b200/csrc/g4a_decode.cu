@@ -1008,12 +1008,14 @@ bool paged_fast_ok(uint32_t page_size, uint32_t hd) {
 
 template <int HD, bool SHORT>
 g4a_status configure_kernel(g4a_ctx* ctx) {
-  static bool done[64] = {false};
-  if (ctx->device < 64 && done[ctx->device]) return G4A_OK;
+  // Per-device flags, atomic because several host threads may make their first call at once
+  // (setting the attribute twice is harmless).
+  static std::atomic<bool> done[64];
+  if (ctx->device < 64 && done[ctx->device].load(std::memory_order_acquire)) return G4A_OK;
   cudaError_t e = cudaFuncSetAttribute(decode_splitkv_kernel<HD, SHORT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)Cfg<HD, SHORT>::SMEM);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(decode_splitkv_kernel)");
-  if (ctx->device < 64) done[ctx->device] = true;
+  if (ctx->device < 64) done[ctx->device].store(true, std::memory_order_release);
   return G4A_OK;
 }
 
@@ -1217,7 +1219,9 @@ constexpr int kMaxDevices = 64;
 std::atomic<void*> g_noalloc_address[kMaxDevices];
 
 // Device address of g4a_noalloc_scratch on `device`, looked up once per device with that device
-// current (the caller's current device is restored afterwards).
+// current (the caller's current device is restored afterwards, and a failure to restore it is
+// reported).  The address is cached for the life of the process; it does not survive a
+// cudaDeviceReset of that device.
 g4a_status noalloc_scratch_address(int device, void** out) {
   if (device < 0 || device >= kMaxDevices) return g4a_fail(G4A_EINVAL, "noalloc scratch: device %d out of range", device);
   void* ptr = g_noalloc_address[device].load(std::memory_order_acquire);
@@ -1226,8 +1230,9 @@ g4a_status noalloc_scratch_address(int device, void** out) {
     G4A_CUDA_TRY(cudaGetDevice(&prev));
     if (prev != device) G4A_CUDA_TRY(cudaSetDevice(device));
     cudaError_t e = cudaGetSymbolAddress(&ptr, g4a_noalloc_scratch);
-    if (prev != device) cudaSetDevice(prev);
+    const cudaError_t restore = (prev != device) ? cudaSetDevice(prev) : cudaSuccess;
     if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaGetSymbolAddress(g4a_noalloc_scratch)");
+    if (restore != cudaSuccess) return g4a_cuda_fail(restore, "cudaSetDevice (restoring the caller's device)");
     if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 255u) != 0)
       return g4a_fail(G4A_ECUDA, "noalloc scratch: unexpected symbol address %p", ptr);
     g_noalloc_address[device].store(ptr, std::memory_order_release);

@@ -148,8 +148,10 @@ g4a_status g4a_decode_attn(g4a_ctx* ctx, const float* q, const uint16_t* k_cache
                            uint32_t sliding_window);
 
 /* g4a_decode_attn without any memory allocation (no counterpart in the reference).  For
- * callers that must not allocate device memory inside the call: a serving loop that captures
- * it into a CUDA graph, or a host whose device-memory budget is fixed up front.  Same arguments,
+ * callers that cannot call cudaMalloc while decoding: an engine that sizes every device buffer
+ * once at load time and owns all device memory from then on (the reference engine creates all
+ * of its work buffers when the model loads), or a process held to a fixed device-memory budget
+ * where an allocation in the middle of generation may fail or stall the device.  Same arguments,
  * semantics and results as g4a_decode_attn; its split-KV scratch is a fixed 4 MiB
  * statically allocated device area instead of the context's workspace, which g4a_decode_attn
  * grows with cudaMalloc.  The area fits every shape with num_kv_heads <= 64 and head_dim <= 512

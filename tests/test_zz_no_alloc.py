@@ -1,10 +1,11 @@
-"""The allocation-free decode entry (g4a_decode_attn_noalloc) against g4a_decode_attn.
+"""The allocation-free decode entry (g4a_decode_attn_noalloc) against g4a_decode_attn and the oracle.
 
 It runs the same kernels with the split-KV scratch in a fixed static device area instead of
 the context's growable workspace, so its output must agree with g4a_decode_attn on the same
-inputs (within the attention tolerance: max abs <= 2e-3, per-head cosine >= 0.9999), on two
-calls in a row, and calls after the first must not change the device's free memory.  The file
-builds all its own state, so it passes alone in a fresh process as well as after the others.
+inputs, and both with the fp64-accumulated CPU oracle (orc_decode_attn_f64), within the
+attention tolerance (max abs <= 2e-3, per-head cosine >= 0.9999), on two calls in a row; calls
+after the first must not change the device's free memory.  The file builds all its own state,
+so it passes alone in a fresh process as well as after the others.
 """
 import numpy as np
 import pytest
@@ -36,7 +37,7 @@ def _inputs(seed, L, hd, nkh):
 
 
 @pytest.mark.parametrize("L,W,hd,nkh", SHAPES)
-def test_noalloc_matches_decode_attn(L, W, hd, nkh):
+def test_noalloc_matches_decode_attn(L, W, hd, nkh, oracle):
     q, k, v = _inputs(L * 7 + hd + nkh, L, hd, nkh)
     kw = dict(num_q_heads=8 * nkh, num_kv_heads=nkh, head_dim=hd, seq_len=L, sliding_window=W, scale=1.0)
     with g4attn.Context(0) as ctx:
@@ -57,6 +58,13 @@ def test_noalloc_matches_decode_attn(L, W, hd, nkh):
         free_after = torch.cuda.mem_get_info()[0]
         got = [o.cpu().numpy() for o in outs]
     assert free_after == free_before, (free_before, free_after)
+    gold = None
+    if L > 0:
+        gold = oracle.decode_attn_f64(q.cpu().numpy(), k.cpu().numpy().view(np.uint16), v.cpu().numpy().view(np.uint16),
+                                      num_q_heads=8 * nkh, num_kv_heads=nkh, head_dim=hd, kv_len=L,
+                                      sliding_window=W).astype(np.float64)
+        r = attention_parity(want, gold)
+        assert r["ok"], ("g4a_decode_attn vs oracle", r)
     for i, g in enumerate(got):
         assert np.isfinite(g).all(), i
         if L == 0:
@@ -64,6 +72,8 @@ def test_noalloc_matches_decode_attn(L, W, hd, nkh):
             continue
         r = attention_parity(g, want.astype(np.float64))
         assert r["ok"], (i, r)
+        r = attention_parity(g, gold)
+        assert r["ok"], (i, "vs oracle", r)
 
 
 def test_noalloc_rejects_shape_beyond_scratch():
