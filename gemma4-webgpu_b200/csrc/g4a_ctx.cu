@@ -195,6 +195,7 @@ g4a_status g4a_destroy(g4a_ctx* ctx) {
   if (ctx == nullptr) return G4A_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  g4a_dist_release(ctx);
   for (auto& r : ctx->prof_pending) {
     cudaEventDestroy(r.begin);
     cudaEventDestroy(r.end);
@@ -232,8 +233,12 @@ g4a_status g4a_sync(g4a_ctx* ctx, uint32_t timeout_ms) {
     cudaError_t e = cudaEventQuery(ctx->sync_event);
     if (e == cudaSuccess) break;
     if (e != cudaErrorNotReady) return g4a_cuda_fail(e, "g4a_sync");
-    if (std::chrono::steady_clock::now() >= deadline)
-      return g4a_fail(G4A_ETIMEOUT, "g4a_sync: work still running after %u ms", timeout_ms);
+    const bool late = std::chrono::steady_clock::now() >= deadline;
+    // a pending collective that failed or outlived the deadline: abort the communicator (its
+    // kernels stop) and report, as the reference turns a lost device into an error
+    if (ctx->nccl_comm != nullptr)
+      if (g4a_status s = g4a_dist_check(ctx, late, timeout_ms)) return s;
+    if (late) return g4a_fail(G4A_ETIMEOUT, "g4a_sync: work still running after %u ms", timeout_ms);
     std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
   int derr = *ctx->dev_err_host;

@@ -57,6 +57,12 @@ struct g4a_ctx {
   cudaEvent_t sync_event = nullptr;
   // Tensor-map encoder from the driver (for the prefill kernel), resolved on first use.
   void* encode_tiled = nullptr;
+  // NCCL communicator of g4a_dist_init (an ncclComm_t), its rank and size; dist_aborted is set
+  // when a deadline or an asynchronous error aborted it.
+  void* nccl_comm = nullptr;
+  int dist_rank = -1;
+  int dist_nranks = 0;
+  bool dist_aborted = false;
   // Profiler state: pending event pairs, free events, per-label totals.
   bool prof_enabled = false;
   std::vector<g4a_prof_rec> prof_pending;
@@ -80,6 +86,10 @@ g4a_status g4a_fail(g4a_status st, const char* fmt, ...);
 g4a_status g4a_cuda_fail(cudaError_t e, const char* what);
 g4a_status g4a_check_launch(const char* what);
 g4a_status g4a_ensure_workspace(g4a_ctx* ctx, size_t bytes);
+// Communicator checks of g4a_sync (g4a_dist.cu): an asynchronous NCCL error, or the deadline
+// passing while a communicator exists, aborts the communicator and returns the error.
+g4a_status g4a_dist_check(g4a_ctx* ctx, bool deadline_passed, uint32_t timeout_ms);
+void g4a_dist_release(g4a_ctx* ctx);
 // Prefill through the decode kernels (shapes the tensor-core prefill kernel does not cover).
 // head_dim 512 prefill with 8 q heads per kv head (g4a_prefill_wide.cu).
 g4a_status prefill_wide(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,

@@ -15,11 +15,26 @@ from ctypes import c_void_p
 from . import _lib
 from ._lib import G4AError, call, exported_symbols, load  # noqa: F401
 
-__all__ = ["Context", "G4AError", "load", "exported_symbols", "version"]
+__all__ = ["Context", "G4AError", "load", "exported_symbols", "version", "dist_unique_id", "dist_poll_selftest"]
 
 
 def version() -> str:
     return load().g4a_version().decode()
+
+
+def dist_unique_id() -> bytes:
+    """A new NCCL unique id (g4a_dist_unique_id): rank 0 makes it and sends it to every rank."""
+    buf = (ctypes.c_uint8 * _lib.DIST_ID_BYTES)()
+    call("g4a_dist_unique_id", ctypes.cast(buf, c_void_p))
+    return bytes(buf)
+
+
+def dist_poll_selftest(scenario: int, timeout_ms: int) -> tuple[int, int]:
+    """Run the communicator deadline logic against the library's fake NCCL (no GPU needed);
+    returns (status, aborted)."""
+    ab = ctypes.c_int(0)
+    st = load().g4a_dist_poll_selftest(int(scenario), int(timeout_ms), ctypes.byref(ab))
+    return int(st), int(ab.value)
 
 
 def _ptr(t) -> c_void_p:
@@ -281,6 +296,53 @@ class Context:
         arr = (c_void_p * len(rank_buffers))(*[c_void_p(b) for b in rank_buffers])
         call("g4a_splitkv_exchange_merge", self._h, _ptr(part), arr, len(rank_buffers), int(rank), int(seq),
              num_q_heads, head_dim, _ptr(out))
+
+    # ---------------------------------------------------------------- multi-GPU over NCCL
+    def dist_init(self, rank: int, nranks: int, unique_id: bytes, timeout_ms: int = 60000) -> None:
+        """Create this context's NCCL communicator (g4a_dist_init, non-blocking, deadline)."""
+        if len(unique_id) != _lib.DIST_ID_BYTES:
+            raise ValueError(f"unique_id must be {_lib.DIST_ID_BYTES} bytes")
+        buf = (ctypes.c_uint8 * _lib.DIST_ID_BYTES).from_buffer_copy(unique_id)
+        call("g4a_dist_init", self._h, int(rank), int(nranks), ctypes.cast(buf, c_void_p), int(timeout_ms))
+
+    def dist_destroy(self) -> None:
+        call("g4a_dist_destroy", self._h)
+
+    def dist_info(self) -> tuple[int, int]:
+        r, n = ctypes.c_int(-1), ctypes.c_int(0)
+        call("g4a_dist_info", self._h, ctypes.byref(r), ctypes.byref(n))
+        return r.value, n.value
+
+    def allgather_partials(self, part, parts_all, floats_per_rank: int, timeout_ms: int = 60000) -> None:
+        import torch
+
+        _check(part, "part", torch.float32, floats_per_rank, self.device)
+        _check(parts_all, "parts_all", torch.float32, None, self.device)
+        call("g4a_allgather_partials", self._h, _ptr(part), _ptr(parts_all), int(floats_per_rank), int(timeout_ms))
+
+    def decode_attn_splitkv(self, q, k_slice, v_slice, parts_all, out, *, num_q_heads, num_kv_heads, head_dim,
+                            kv_begin, kv_end, kv_len_total, scale=1.0, sliding_window=0, timeout_ms=60000) -> None:
+        """One split-KV step on this rank: partial of its slice, NCCL all-gather, merge (g4a_decode_attn_splitkv)."""
+        import torch
+
+        _check(q, "q", torch.float32, num_q_heads * head_dim, self.device)
+        _check(k_slice, "k_slice", torch.float16, None, self.device)
+        _check(v_slice, "v_slice", torch.float16, None, self.device)
+        _check(parts_all, "parts_all", torch.float32, None, self.device)
+        _check(out, "out", torch.float32, num_q_heads * head_dim, self.device)
+        call("g4a_decode_attn_splitkv", self._h, _ptr(q), _ptr(k_slice), _ptr(v_slice), num_q_heads, num_kv_heads,
+             head_dim, int(kv_begin), int(kv_end), int(kv_len_total), float(scale), int(sliding_window),
+             _ptr(parts_all), _ptr(out), int(timeout_ms))
+
+    def dist_allgather_host(self, data: bytes, timeout_ms: int = 60000) -> list[bytes]:
+        """Synchronous all-gather of equal-sized byte strings over the communicator."""
+        n = self.dist_info()[1]
+        send = (ctypes.c_uint8 * len(data)).from_buffer_copy(data)
+        recv = (ctypes.c_uint8 * (len(data) * max(n, 1)))()
+        call("g4a_dist_allgather_host", self._h, ctypes.cast(send, c_void_p), ctypes.cast(recv, c_void_p), len(data),
+             int(timeout_ms))
+        raw = bytes(recv)
+        return [raw[i * len(data):(i + 1) * len(data)] for i in range(n)]
 
     # ---------------------------------------------------------------- projections
     def matmul(self, weight_format: int, x, weight, scales, out, *, M: int, N: int) -> None:

@@ -37,6 +37,7 @@ class G4AError(RuntimeError):
 
 WEIGHT_F16, WEIGHT_Q8, WEIGHT_Q4K = 0, 1, 2  # G4A_WEIGHT_* of g4a_matmul
 MATMUL_MAX_JOBS = 4
+DIST_ID_BYTES = 128  # G4A_DIST_ID_BYTES
 
 
 class MatmulJob(ctypes.Structure):
@@ -83,6 +84,14 @@ SIGNATURES: dict[str, list] = {
     "g4a_ipc_open_handle": [_p, _p, POINTER(c_void_p)],
     "g4a_ipc_close_handle": [_p, _p],
     "g4a_splitkv_exchange_merge": [_p, _p, POINTER(c_void_p), _u32, _u32, _u32, _u32, _u32, _p],
+    "g4a_dist_unique_id": [_p],
+    "g4a_dist_init": [_p, c_int, c_int, _p, _u32],
+    "g4a_dist_destroy": [_p],
+    "g4a_dist_info": [_p, POINTER(c_int), POINTER(c_int)],
+    "g4a_allgather_partials": [_p, _p, _p, c_size_t, _u32],
+    "g4a_decode_attn_splitkv": [_p, _p, _p, _p, _u32, _u32, _u32, _u32, _u32, _u32, _f, _u32, _p, _p, _u32],
+    "g4a_dist_allgather_host": [_p, _p, _p, c_size_t, _u32],
+    "g4a_dist_poll_selftest": [c_int, _u32, POINTER(c_int)],
     "g4a_matmul": [_p, _u32, _p, _p, _p, _p, _u32, _u32],
     "g4a_matmul_group": [_p, _u32, _p, _u32, POINTER(MatmulJob), _u32],
 }

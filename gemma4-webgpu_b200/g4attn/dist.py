@@ -10,8 +10,11 @@ Two partitionings, both one process per GPU:
   the partials (8 * (head_dim + 2) floats per rank) are all-gathered over NCCL with
   ``torch.distributed``, and every rank runs the log-sum-exp merge kernel ``g4a_lse_merge``.
 
-Collective plumbing uses torch.distributed (NCCL on GPUs, gloo for the CPU tests); the numeric
-work stays in libg4attn.so.
+Collective plumbing: either torch.distributed (NCCL on GPUs, gloo for the CPU tests), or the
+library's own communicator through its C ABI (``g4a_dist_init`` / ``g4a_decode_attn_splitkv`` /
+``g4a_dist_allgather_host``: ``CabiSplitKVDecoder`` and ``CabiPeerSplitKVDecoder``), which needs
+no torch.distributed at all -- the path a TypeScript / N-API host uses.  The numeric work stays
+in libg4attn.so either way.
 """
 from __future__ import annotations
 
@@ -141,25 +144,43 @@ class PeerSplitKVDecoder:
         self.nqh = num_q_heads
         self.hd = head_dim
         self.seq = 0
+        self._setup(load, num_q_heads, head_dim)
+
+    def _allgather_bytes(self, data: bytes) -> list[bytes]:
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor(list(data), dtype=torch.uint8)
+        if dist.get_backend(self.group) == "nccl":
+            t = t.cuda(self.ctx.device)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t, group=self.group)
+        return [bytes(x.cpu().tolist()) for x in out]
+
+    def _barrier(self) -> None:
+        import torch.distributed as dist
+
+        dist.barrier(group=self.group)
+
+    def _setup(self, load, num_q_heads: int, head_dim: int) -> None:
+        import torch
+
+        ctx = self.ctx
         nbytes = int(load().g4a_exchange_buffer_bytes(self.world, num_q_heads, head_dim))
         self.own = ctx.alloc(nbytes)
         ctx.memset(self.own, 0, nbytes)
         ctx.sync()
-        handle = torch.tensor(list(ctx.ipc_handle(self.own)), dtype=torch.uint8)
-        if dist.get_backend(group) == "nccl":
-            handle = handle.cuda(ctx.device)
-        handles = [torch.zeros_like(handle) for _ in range(self.world)]
-        dist.all_gather(handles, handle, group=group)
+        handles = self._allgather_bytes(ctx.ipc_handle(self.own))
         self.opened = []
         self.buffers = []
         for r, h in enumerate(handles):
             if r == self.rank:
                 self.buffers.append(self.own)
             else:
-                p = ctx.ipc_open(bytes(h.cpu().tolist()))
+                p = ctx.ipc_open(h)
                 self.opened.append(p)
                 self.buffers.append(p)
-        dist.barrier(group=group)
+        self._barrier()
         dev = torch.device("cuda", ctx.device)
         self.part = torch.empty(partial_floats(num_q_heads, head_dim), dtype=torch.float32, device=dev)
 
@@ -174,14 +195,64 @@ class PeerSplitKVDecoder:
         return out
 
     def close(self) -> None:
-        import torch.distributed as dist
-
         self.ctx.sync()
-        dist.barrier(group=self.group)  # nobody writes into a buffer after this point
+        self._barrier()  # nobody writes into a buffer after this point
         for p in self.opened:
             self.ctx.ipc_close(p)
         self.opened = []
-        dist.barrier(group=self.group)
+        self._barrier()
         if self.own:
             self.ctx.free(self.own)
             self.own = 0
+
+
+class CabiPeerSplitKVDecoder(PeerSplitKVDecoder):
+    """``PeerSplitKVDecoder`` bootstrapped over the context's own communicator (``ctx.dist_init``
+    done by the caller): the IPC handles travel with ``g4a_dist_allgather_host`` and the barriers
+    are one-byte all-gathers, so no torch.distributed is involved."""
+
+    def __init__(self, ctx, num_q_heads: int = 8, head_dim: int = 256, timeout_ms: int = 60000):
+        from ._lib import load
+
+        self.ctx = ctx
+        self.group = None
+        self.rank, self.world = ctx.dist_info()
+        if self.world < 1:
+            raise ValueError("the context has no communicator: call ctx.dist_init first")
+        self.nqh = num_q_heads
+        self.hd = head_dim
+        self.seq = 0
+        self.timeout_ms = timeout_ms
+        self._setup(load, num_q_heads, head_dim)
+
+    def _allgather_bytes(self, data: bytes) -> list[bytes]:
+        return self.ctx.dist_allgather_host(data, self.timeout_ms)
+
+    def _barrier(self) -> None:
+        self.ctx.dist_allgather_host(b"\x01", self.timeout_ms)
+
+
+class CabiSplitKVDecoder:
+    """Long-context split-KV decode through the C ABI alone: ``g4a_decode_attn_splitkv`` computes
+    the partial of this rank's slice, all-gathers the partials over the context's NCCL
+    communicator (``ctx.dist_init``, non-blocking with deadlines) and merges them."""
+
+    def __init__(self, ctx, num_q_heads: int = 8, head_dim: int = 256, timeout_ms: int = 60000):
+        import torch
+
+        self.ctx = ctx
+        self.rank, self.world = ctx.dist_info()
+        if self.world < 1:
+            raise ValueError("the context has no communicator: call ctx.dist_init first")
+        self.nqh = num_q_heads
+        self.hd = head_dim
+        self.timeout_ms = timeout_ms
+        dev = torch.device("cuda", ctx.device)
+        self.parts_all = torch.empty(self.world * partial_floats(num_q_heads, head_dim), dtype=torch.float32,
+                                     device=dev)
+
+    def step(self, q, k_slice, v_slice, out, *, begin, end, kv_len_total, scale=1.0, sliding_window=0):
+        self.ctx.decode_attn_splitkv(q, k_slice, v_slice, self.parts_all, out, num_q_heads=self.nqh, num_kv_heads=1,
+                                     head_dim=self.hd, kv_begin=begin, kv_end=end, kv_len_total=kv_len_total,
+                                     scale=scale, sliding_window=sliding_window, timeout_ms=self.timeout_ms)
+        return out

@@ -49,7 +49,7 @@ typedef enum {
   G4A_ECUDA = 2,        /* CUDA runtime / launch / device error */
   G4A_ENOMEM = 3,       /* device allocation failed */
   G4A_ETIMEOUT = 4,     /* g4a_sync deadline passed, or a kernel's bounded wait gave up */
-  G4A_ENCCL = 5,        /* reserved for collective errors reported through this ABI */
+  G4A_ENCCL = 5,        /* a collective failed (NCCL error; the communicator was aborted) */
   G4A_EUNSUPPORTED = 6  /* valid request that this build does not implement */
 } g4a_status;
 
@@ -272,7 +272,8 @@ g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k
  * WebGPU device).  One process per GPU.  Each rank allocates one exchange buffer of
  * g4a_exchange_buffer_bytes(world, num_q_heads, head_dim) bytes with g4a_alloc, zeroes it once
  * with g4a_memset, exports it with g4a_ipc_get_handle, sends the handle to every other rank
- * (e.g. over torch.distributed), and opens the others' handles with g4a_ipc_open_handle.
+ * (g4a_dist_allgather_host below, or any other channel), and opens the others' handles with
+ * g4a_ipc_open_handle.
  * Every step, every rank calls g4a_splitkv_exchange_merge with the same `seq` (1, 2, 3, ...):
  * it stores this rank's partial (the m | l | o layout of g4a_decode_attn_partial) into slot
  * `rank` of every rank's buffer, raises its flag there, waits until every rank's partial of
@@ -289,6 +290,49 @@ g4a_status g4a_ipc_close_handle(g4a_ctx* ctx, void* dptr);
 g4a_status g4a_splitkv_exchange_merge(g4a_ctx* ctx, const float* part, void* const* rank_buffers,
                                       uint32_t world, uint32_t rank, uint32_t seq,
                                       uint32_t num_q_heads, uint32_t head_dim, float* out);
+
+/* ------------------------------------------------------------------ multi-GPU over NCCL */
+
+/* Split-KV decode of one long context over N GPUs through this ABI alone (no PyTorch): one
+ * process and one context per GPU, an NCCL communicator per context.  The reference decodes one
+ * sequence on one WebGPU device and has no collective; its failure handling -- a lost device
+ * turns into an error at the next call (src/engine.ts:432-435, 2214, 2509) -- is what the
+ * deadlines below mirror.  NCCL (libnccl.so.2) is loaded when first needed; without it these
+ * calls return G4A_EUNSUPPORTED.
+ *
+ * g4a_dist_unique_id: rank 0 creates the 128-byte id and sends it to every rank out of band.
+ * g4a_dist_init: creates the context's communicator (ncclCommInitRankConfig, non-blocking) and
+ *   waits for all ranks to join; if they have not after timeout_ms, or NCCL reports an error,
+ *   the communicator is aborted and G4A_ETIMEOUT / G4A_ENCCL returned.
+ * g4a_allgather_partials: enqueues ncclAllGather of floats_per_rank floats from `part` into
+ *   parts_all [nranks * floats_per_rank] on the context's stream (part may be the rank's own
+ *   slot of parts_all).  Completion is observed by g4a_sync, which also watches the communicator:
+ *   an asynchronous NCCL error, or the sync deadline passing with the collective still pending
+ *   (a rank that never joined), aborts the communicator -- its kernels stop -- and returns
+ *   G4A_ENCCL / G4A_ETIMEOUT.  After an abort, dist calls fail until g4a_dist_init is called again.
+ * g4a_decode_attn_splitkv: the whole step on this rank -- g4a_decode_attn_partial over its slice
+ *   (k_slice / v_slice hold positions [kv_begin, kv_end) of a kv_len_total-long cache), the
+ *   all-gather into parts_all (device, nranks * num_q_heads * (head_dim + 2) floats) and
+ *   g4a_lse_merge into out [num_q_heads, head_dim].  One kv head per call.
+ * g4a_dist_allgather_host: a synchronous all-gather of `bytes` host bytes from every rank into
+ *   recv [nranks * bytes] (bootstrap of the peer-exchange IPC handles without another channel).
+ * g4a_dist_destroy: releases the communicator (also done by g4a_destroy).
+ * g4a_dist_poll_selftest: runs the deadline logic of these calls against a built-in fake of NCCL
+ *   -- scenario 0: the operation completes on the third poll, 1: a rank never joins, 2: a peer
+ *   fails -- without a GPU or NCCL; *aborted = 1 when the fake communicator was aborted once. */
+#define G4A_DIST_ID_BYTES 128
+g4a_status g4a_dist_unique_id(void* id_out);
+g4a_status g4a_dist_init(g4a_ctx* ctx, int rank, int nranks, const void* id, uint32_t timeout_ms);
+g4a_status g4a_dist_destroy(g4a_ctx* ctx);
+g4a_status g4a_dist_info(g4a_ctx* ctx, int* rank, int* nranks);
+g4a_status g4a_allgather_partials(g4a_ctx* ctx, const float* part, float* parts_all, size_t floats_per_rank,
+                                  uint32_t timeout_ms);
+g4a_status g4a_decode_attn_splitkv(g4a_ctx* ctx, const float* q, const uint16_t* k_slice, const uint16_t* v_slice,
+                                   uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t head_dim, uint32_t kv_begin,
+                                   uint32_t kv_end, uint32_t kv_len_total, float scale, uint32_t sliding_window,
+                                   float* parts_all, float* out, uint32_t timeout_ms);
+g4a_status g4a_dist_allgather_host(g4a_ctx* ctx, const void* send, void* recv, size_t bytes, uint32_t timeout_ms);
+g4a_status g4a_dist_poll_selftest(int scenario, uint32_t timeout_ms, int* aborted);
 
 /* ------------------------------------------------------------------ projections (GEMV) */
 
