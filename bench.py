@@ -508,76 +508,96 @@ def _max_over_ranks(torch, dist, value: float) -> float:
     return float(t.item())
 
 
+def _time_batched(ctx, torch, lens, seed: int) -> float:
+    """Device us per step (one sliding + one global paged decode over the sequences `lens`)."""
+    import numpy as np
+
+    from g4attn import synth
+
+    B = len(lens)
+    if B == 0:
+        return 0.0
+    g = torch.Generator(device="cuda")
+    g.manual_seed(40 + seed)
+    layers = []
+    for li in range(2):
+        table, npages = synth.page_assignment(7 + li + 100 * seed, lens, 64)
+        kp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+        vp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+        layers.append((kp, vp, torch.from_numpy(table).cuda(), npages))
+    q = torch.randn((B, NQH, HD), generator=g, device="cuda")
+    out = torch.empty((B, NQH, HD), device="cuda")
+    kvl = torch.from_numpy(np.asarray(lens, dtype=np.int32)).cuda()
+    ctx.reserve_workspace(B, HD, NQH)
+
+    def step():
+        for li, (kp, vp, table, npages) in enumerate(layers):
+            ctx.decode_attn_paged(q, kp, vp, table, kvl, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                                  page_size=64, sliding_window=512 if li == 0 else 0, host_kv_lens=lens)
+
+    for _ in range(3):
+        step()
+    ctx.sync()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    gr = torch.cuda.CUDAGraph()
+    ctx.set_stream(s.cuda_stream)
+    with torch.cuda.stream(s):
+        gr.capture_begin()
+        step()
+        gr.capture_end()
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    n = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    del gr, layers
+    torch.cuda.empty_cache()
+    return us
+
+
 def run_batched(ctx, torch, rank, world, dist):
     """64 sequences, L ~ U[1024, 32768] (seeded), 64-token pages in a seeded
     random order; a step is one sliding layer (W 512) and one global layer per sequence.  The
     sequences are sharded over ranks by LPT on their KV bytes, with no collective; the time is the
-    max over ranks.  Page contents are seeded N(0,1) f16 (the bandwidth does not depend on them)."""
+    max over ranks.  Page contents are seeded N(0,1) f16 (the bandwidth does not depend on them).
+    The total work is fixed (strong scaling): with N > 1 ranks, rank 0 also times the whole batch
+    alone, and `efficiency` = t(1 GPU) / (N x t(N GPUs))."""
     import numpy as np
 
     from g4attn import dist as gdist
     from g4attn import synth
 
     lengths = synth.batched_lengths(2, 64, 1024, 32768)
-    bins = gdist.lpt_shard(gdist.decode_cost_bytes(lengths) + gdist.decode_cost_bytes(lengths, window=512), world)
+    costs = gdist.decode_cost_bytes(lengths) + gdist.decode_cost_bytes(lengths, window=512)
+    bins = gdist.lpt_shard(costs, world)
     mine = np.array(sorted(bins[rank]), dtype=np.int64)
     lens = lengths[mine].astype(np.int32)
-    B = len(lens)
     total_bytes = sum(kv_bytes(int(L), 512) + kv_bytes(int(L)) for L in lengths)
+    loads = [int(costs[b].sum()) for b in bins]
     res = {"config": "config[2]: B=64, L~U[1k,32k] seed 2, 64-token pages, sliding (W 512) + global layer",
-           "sequences_on_rank0": B}
-    if B == 0:
-        us = 0.0
-    else:
-        g = torch.Generator(device="cuda")
-        g.manual_seed(40 + rank)
-        layers = []
-        for li in range(2):
-            table, npages = synth.page_assignment(7 + li + 100 * rank, lens, 64)
-            kp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
-            vp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
-            layers.append((kp, vp, torch.from_numpy(table).cuda(), npages))
-        q = torch.randn((B, NQH, HD), generator=g, device="cuda")
-        out = torch.empty((B, NQH, HD), device="cuda")
-        kvl = torch.from_numpy(lens).cuda()
-        ctx.reserve_workspace(B, HD, NQH)
-
-        def step():
-            for li, (kp, vp, table, npages) in enumerate(layers):
-                ctx.decode_attn_paged(q, kp, vp, table, kvl, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
-                                      page_size=64, sliding_window=512 if li == 0 else 0, host_kv_lens=lens)
-
-        for _ in range(3):
-            step()
-        ctx.sync()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        gr = torch.cuda.CUDAGraph()
-        ctx.set_stream(s.cuda_stream)
-        with torch.cuda.stream(s):
-            gr.capture_begin()
-            step()
-            gr.capture_end()
-        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
-        n = 50
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(n):
-            gr.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / n
-        del gr, layers
+           "sequences_on_rank0": len(lens)}
+    us = _time_batched(ctx, torch, lens, rank)
     if dist:
         dist.barrier()
     us = _max_over_ranks(torch, dist, us)
+    us1 = us
+    if world > 1:
+        us1 = _time_batched(ctx, torch, lengths.astype(np.int32), 0) if rank == 0 else 0.0
+        dist.barrier()
     hbm, _, _ = peaks()
     res.update({"us_per_step": us, "GB/s": total_bytes / (us * 1e-6) / 1e9 if us else None,
                 "bytes_per_step": total_bytes, "frac_of_measured_hbm_per_gpu":
                     (total_bytes / (us * 1e-6) / 1e9) / world / hbm if us else None,
-                "sharding": f"LPT over {world} rank(s), no collective"})
-    torch.cuda.empty_cache()
+                "sharding": f"LPT over {world} rank(s), no collective",
+                "us_per_step_1gpu": us1, "efficiency": us1 / (world * us) if us else None,
+                "lpt_imbalance": max(loads) / (sum(loads) / len(loads)),
+                "limiter": "per-rank fixed cost per call and LPT imbalance (no data-path collective)"})
     return res
 
 
@@ -616,11 +636,21 @@ def run_splitkv(ctx, torch, rank, world, dist):
     total = kv_bytes(L)
     hbm, _, _ = peaks()
     if dist:
+        import g4attn
+
         # the library's exchange over NVLink peer memory (the product path) ...
         peer = gdist.PeerSplitKVDecoder(ctx)
         us = timed(lambda: peer.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L))
         peer.close()
-        # ... and, for comparison, NCCL all_gather + the lse merge kernel
+        # ... the C-ABI communicator (g4a_decode_attn_splitkv: NCCL all-gather + merge kernel) ...
+        uid = [g4attn.dist_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.dist_init(rank, world, uid[0], 60000)
+        cabi = gdist.CabiSplitKVDecoder(ctx, timeout_ms=60000)
+        res["cabi_nccl_us_per_layer"] = timed(lambda: cabi.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L))
+        ctx.sync()
+        ctx.dist_destroy()
+        # ... and torch.distributed's NCCL all_gather + the lse merge kernel
         nccl = gdist.SplitKVDecoder(ctx)
         res["nccl_allgather_us_per_layer"] = timed(lambda: nccl.step(q, kc, vc, out, begin=b, end=e, kv_len_total=L))
         res["exchange"] = "partials pushed to every rank over NVLink peer memory by one exchange+merge kernel"
@@ -630,8 +660,31 @@ def run_splitkv(ctx, torch, rank, world, dist):
         res["exchange"] = "none (one rank)"
     del kc, vc
     torch.cuda.empty_cache()
+    # fixed total work (strong scaling): rank 0 also decodes the whole 1M cache alone
+    us1 = us
+    if dist:
+        us1 = 0.0
+        if rank == 0:
+            kf = torch.randn((L, NKH, HD), generator=g, device="cuda").half()
+            vf = torch.randn((L, NKH, HD), generator=g, device="cuda").half()
+            for _ in range(3):
+                ctx.decode_attn(q, kf, vf, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(20):
+                ctx.decode_attn(q, kf, vf, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD, seq_len=L)
+            e1.record()
+            torch.cuda.synchronize()
+            us1 = e0.elapsed_time(e1) * 1e3 / 20
+            del kf, vf
+            torch.cuda.empty_cache()
+        dist.barrier()
     res.update({"us_per_layer": us, "GB/s": total / (us * 1e-6) / 1e9,
-                "frac_of_measured_hbm_per_gpu": total / (us * 1e-6) / 1e9 / world / hbm})
+                "frac_of_measured_hbm_per_gpu": total / (us * 1e-6) / 1e9 / world / hbm,
+                "us_per_layer_1gpu": us1, "efficiency": us1 / (world * us),
+                "limiter": "streaming of each rank's slice plus one exchange round trip (flag release/acquire "
+                           "over NVLink) and the merge" if world > 1 else "HBM streaming"})
     return res
 
 

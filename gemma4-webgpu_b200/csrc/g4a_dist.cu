@@ -88,7 +88,8 @@ g4a_status nccl_wait(const NcclApi& api, ncclComm_t comm, ncclResult_t first, ui
                      bool* aborted) {
   *aborted = false;
   ncclResult_t st = first;
-  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  const auto t0 = std::chrono::steady_clock::now();
+  const auto deadline = t0 + std::chrono::milliseconds(timeout_ms);
   while (true) {
     if (st == ncclSuccess) return G4A_OK;
     if (st != ncclInProgress) {
@@ -102,7 +103,11 @@ g4a_status nccl_wait(const NcclApi& api, ncclComm_t comm, ncclResult_t first, ui
       return g4a_fail(G4A_ETIMEOUT, "%s: not complete after %u ms (a rank did not join); the communicator was aborted",
                       what, timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    // an enqueue normally completes within microseconds: spin for the first 2 ms, then back off
+    if (std::chrono::steady_clock::now() - t0 < std::chrono::milliseconds(2))
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
     const ncclResult_t q = api.commGetAsyncError(comm, &st);
     if (q != ncclSuccess && q != ncclInProgress) st = q;
   }
