@@ -133,44 +133,114 @@ __device__ __forceinline__ StepRaw<FMT> load_step(const GemvJob& jb, uint32_t m,
   return r;
 }
 
-// acc[e] += term(element 256 j + 8 lane + e) for the lane's eight threads.
+// Packed pairs of f32 for the sm_100 two-lane FP32 instructions (add / sub / mul / fma .rn.f32x2):
+// each rounds both halves exactly like the scalar instruction, so pairing elements halves the
+// instruction count of the per-element terms without changing a bit.  Low half = first element.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// The partial sums of a lane's eight threads t = 8 lane + e, as pairs (e = 2i, 2i + 1).
+struct Acc8 {
+  uint64_t p[4];
+};
+
+// acc[e] += term(element 256 j + 8 lane + e) for the lane's eight threads, two elements per
+// instruction (every product and sum still separately rounded, in the shader's order).
 template <uint32_t FMT>
 __device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, int lane, const float* xs,
-                                             float (&acc)[8]) {
+                                             Acc8& acc) {
   const uint32_t k0 = 256u * j + 8u * (uint32_t)lane;
-  const float4 xa = *reinterpret_cast<const float4*>(xs + k0);
-  const float4 xb = *reinterpret_cast<const float4*>(xs + k0 + 4);
-  const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  const ulonglong2 xa = *reinterpret_cast<const ulonglong2*>(xs + k0);
+  const ulonglong2 xb = *reinterpret_cast<const ulonglong2*>(xs + k0 + 4);
+  const uint64_t x[4] = {xa.x, xa.y, xb.x, xb.y};
   if constexpr (FMT == G4A_WEIGHT_F16) {
+    // scalar: this path streams at the copy rate already, and the paired form of f32(w) * x + acc
+    // did not keep the shader's separate roundings
     const uint32_t w4[4] = {r.w.x, r.w.y, r.w.z, r.w.w};
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const __half h = __ushort_as_half((unsigned short)(w4[e / 2] >> (16 * (e & 1))));
-      acc[e] = __fadd_rn(acc[e], __fmul_rn(__half2float(h), x[e]));
+    for (int i = 0; i < 4; i++) {
+      const float2 w = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+      const float2 xv = f2_unpack(x[i]);
+      float2 a = f2_unpack(acc.p[i]);
+      a.x = __fadd_rn(a.x, __fmul_rn(w.x, xv.x));
+      a.y = __fadd_rn(a.y, __fmul_rn(w.y, xv.y));
+      acc.p[i] = f2_pack(a.x, a.y);
     }
   } else if constexpr (FMT == G4A_WEIGHT_Q8) {
     // int8 q as the byte u = q + 128 (flip the sign bit of every byte): 2^23 + u - (2^23 + 128)
     const float sc = __half2float(r.sc);
+    const uint64_t sc2 = f2_pack(sc, sc), bias2 = f2_pack(8388736.0f, 8388736.0f);
     const uint32_t u0 = r.w.x ^ 0x80808080u, u1 = r.w.y ^ 0x80808080u;
-    const float q[8] = {byte_biased<0>(u0), byte_biased<1>(u0), byte_biased<2>(u0), byte_biased<3>(u0),
-                        byte_biased<0>(u1), byte_biased<1>(u1), byte_biased<2>(u1), byte_biased<3>(u1)};
+    const uint64_t q[4] = {f2_pack(byte_biased<0>(u0), byte_biased<1>(u0)),
+                           f2_pack(byte_biased<2>(u0), byte_biased<3>(u0)),
+                           f2_pack(byte_biased<0>(u1), byte_biased<1>(u1)),
+                           f2_pack(byte_biased<2>(u1), byte_biased<3>(u1))};
 #pragma unroll
-    for (int e = 0; e < 8; e++)
-      acc[e] = __fadd_rn(acc[e], __fmul_rn(__fmul_rn(__fsub_rn(q[e], 8388736.0f), sc), x[e]));
+    for (int i = 0; i < 4; i++) {
+      const float2 t = f2_unpack(f2_mul(f2_mul(f2_sub(q[i], bias2), sc2), x[i]));
+      float2 a = f2_unpack(acc.p[i]);
+      a.x = __fadd_rn(a.x, t.x);
+      a.y = __fadd_rn(a.y, t.y);
+      acc.p[i] = f2_pack(a.x, a.y);
+    }
   } else {
     // Nibbles 0, 2, 4, 6 are the bytes of `lo`, nibbles 1, 3, 5, 7 those of `hi`.
     const uint32_t lo = r.w & 0x0F0F0F0Fu, hi = (r.w >> 4) & 0x0F0F0F0Fu;
-    const float nb[8] = {byte_biased<0>(lo), byte_biased<0>(hi), byte_biased<1>(lo), byte_biased<1>(hi),
-                         byte_biased<2>(lo), byte_biased<2>(hi), byte_biased<3>(lo), byte_biased<3>(hi)};
+    const uint64_t nb[4] = {f2_pack(byte_biased<0>(lo), byte_biased<0>(hi)),
+                            f2_pack(byte_biased<1>(lo), byte_biased<1>(hi)),
+                            f2_pack(byte_biased<2>(lo), byte_biased<2>(hi)),
+                            f2_pack(byte_biased<3>(lo), byte_biased<3>(hi))};
     const float sc = __half2float(r.sc), mn = __half2float(r.mn);
+    const uint64_t sc2 = f2_pack(sc, sc), mn2 = f2_pack(mn, mn), bias2 = f2_pack(8388608.0f, 8388608.0f);
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
+    for (int i = 0; i < 4; i++) {
       // The shader's RN(RN(scale * nib) + min) is one fused multiply-add here: scale is an f16
       // value and nib an integer below 16, so their product has at most 15 significant bits
       // within the f32 normal range and is exact; the fma's single rounding is then the sum's.
-      const float wv = __fmaf_rn(sc, __fsub_rn(nb[e], 8388608.0f), mn);
-      acc[e] = __fadd_rn(acc[e], __fmul_rn(wv, x[e]));
+      const uint64_t wv = f2_fma(sc2, f2_sub(nb[i], bias2), mn2);
+      const float2 t = f2_unpack(f2_mul(wv, x[i]));
+      float2 a = f2_unpack(acc.p[i]);
+      a.x = __fadd_rn(a.x, t.x);
+      a.y = __fadd_rn(a.y, t.y);
+      acc.p[i] = f2_pack(a.x, a.y);
     }
+  }
+}
+
+__device__ __forceinline__ void acc_unpack(const Acc8& acc, float (&a)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 v = f2_unpack(acc.p[i]);
+    a[2 * i] = v.x;
+    a[2 * i + 1] = v.y;
   }
 }
 
@@ -263,7 +333,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __re
   auto sum_row = [&](StepRaw<FMT>(&raw)[B], uint32_t row) {
     uint32_t m;
     const GemvJob& jb = job_of(jobs, row, m);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    Acc8 acc = {{0, 0, 0, 0}};  // +0.0f pairs
 #pragma unroll
     for (int u = 0; u < B; u++)
       if ((uint32_t)u < mine) consume_step<FMT>(raw[u], u, lane, xs, acc);
@@ -273,7 +343,9 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __re
       for (int u = 0; u < B; u++)
         if (j + u < mine) consume_step<FMT>(raw[u], j + u, lane, xs, acc);
     }
-    const float v = tree_butterfly(acc, lane);
+    float a[8];
+    acc_unpack(acc, a);
+    const float v = tree_butterfly(a, lane);
     if (lane == 0) jb.out[m] = v;
   };
   if constexpr (kPipe) {
@@ -331,10 +403,12 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float
     }
   };
   auto sum_row = [&](const StepRaw<FMT>(&raw)[S], uint32_t row) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    Acc8 acc = {{0, 0, 0, 0}};  // +0.0f pairs
 #pragma unroll
     for (int u = 0; u < S; u++) consume_step<FMT>(raw[u], (uint32_t)u, lane, xs, acc);
-    const float v = tree_butterfly(acc, lane);
+    float a[8];
+    acc_unpack(acc, a);
+    const float v = tree_butterfly(a, lane);
     uint32_t m;
     const GemvJob& jb = job_of(jobs, row, m);
     if (lane == 0) jb.out[m] = v;
