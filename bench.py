@@ -486,8 +486,10 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    h0 = time.perf_counter()
     for i in range(calls):
         layer_call(i % R)
+    h1 = time.perf_counter()
     e1.record()
     torch.cuda.synchronize()
     ms = _max_over_ranks(torch, dist, e0.elapsed_time(e1))
@@ -495,6 +497,7 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
     return {"value": kv_bytes(L) * calls * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": nb(hqkv), "d2h_bytes_per_step": nb(hout),
             "us_per_layer": ms * 1e3 / calls, "layer_calls_per_rank": calls,
+            "host_enqueue_us_per_call": (h1 - h0) * 1e6 / calls,
             "path": "one g4a_attn_decode_layer_io call per layer call: the producer kernel reads q|k|v "
                     "(10,240 B) from pinned host memory over PCIe, the layer runs (q/k norm+RoPE, v_norm, store, "
                     "attention), the attention writes the output (8,192 B) into pinned host memory"}
