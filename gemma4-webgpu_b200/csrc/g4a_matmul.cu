@@ -172,15 +172,22 @@ struct Acc8 {
   uint64_t p[4];
 };
 
-// acc[e] += term(element 256 j + 8 lane + e) for the lane's eight threads, two elements per
-// instruction (every product and sum still separately rounded, in the shader's order).
-template <uint32_t FMT>
-__device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, int lane, const float* xs,
-                                             Acc8& acc) {
+// The lane's eight input elements of step j (256 j + 8 lane .. + 7) as four pairs.
+__device__ __forceinline__ void load_x_pairs(const float* xs, uint32_t j, int lane, uint64_t (&x)[4]) {
   const uint32_t k0 = 256u * j + 8u * (uint32_t)lane;
   const ulonglong2 xa = *reinterpret_cast<const ulonglong2*>(xs + k0);
   const ulonglong2 xb = *reinterpret_cast<const ulonglong2*>(xs + k0 + 4);
-  const uint64_t x[4] = {xa.x, xa.y, xb.x, xb.y};
+  x[0] = xa.x;
+  x[1] = xa.y;
+  x[2] = xb.x;
+  x[3] = xb.y;
+}
+
+// acc[e] += term(element 256 j + 8 lane + e) for the lane's eight threads, two elements per
+// instruction (every product and sum still separately rounded, in the shader's order); x holds
+// the lane's eight input elements of the step.
+template <uint32_t FMT>
+__device__ __forceinline__ void consume_step_x(const StepRaw<FMT>& r, const uint64_t (&x)[4], Acc8& acc) {
   if constexpr (FMT == G4A_WEIGHT_F16) {
     // scalar: this path streams at the copy rate already, and the paired form of f32(w) * x + acc
     // did not keep the shader's separate roundings
@@ -233,6 +240,14 @@ __device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, 
       acc.p[i] = f2_pack(a.x, a.y);
     }
   }
+}
+
+template <uint32_t FMT>
+__device__ __forceinline__ void consume_step(const StepRaw<FMT>& r, uint32_t j, int lane, const float* xs,
+                                             Acc8& acc) {
+  uint64_t x[4];
+  load_x_pairs(xs, j, lane, x);
+  consume_step_x<FMT>(r, x, acc);
 }
 
 __device__ __forceinline__ void acc_unpack(const Acc8& acc, float (&a)[8]) {
@@ -368,8 +383,8 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_kernel(const float* __re
 // reference model): a lane's row pointer is formed once and every step is a compile-time
 // offset from it, with no per-step bounds predicate.  Q8 and Q4K load the next row's steps
 // while the current row is summed; f16 (twice the registers per step) loads at the row start.
-template <uint32_t FMT, int S>
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float* __restrict__ x,
+template <uint32_t FMT, int S, bool XREG = false>
+__global__ void __launch_bounds__(kGemvThreads, XREG ? 2 : 3) gemv_fixed_kernel(const float* __restrict__ x,
                                                                      const __grid_constant__ GemvJobs jobs) {
   constexpr uint32_t N = 256u * S;
   extern __shared__ float4 gemv_smem[];
@@ -402,10 +417,21 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float
       }
     }
   };
+  // XREG (Q8 and Q4K with many rows): the lane's S x 8 input elements stay in registers across
+  // the warp's rows (the input is the same for every row), so the inner loop reads no shared
+  // memory, at two CTAs per SM instead of three.  Few rows (the per-layer projections) are
+  // latency-bound and keep the shared-memory form.
+  static_assert(!XREG || FMT != G4A_WEIGHT_F16, "XREG is for the quantised formats");
+  uint64_t xr[XREG ? S : 1][4];
   auto sum_row = [&](const StepRaw<FMT>(&raw)[S], uint32_t row) {
     Acc8 acc = {{0, 0, 0, 0}};  // +0.0f pairs
 #pragma unroll
-    for (int u = 0; u < S; u++) consume_step<FMT>(raw[u], (uint32_t)u, lane, xs, acc);
+    for (int u = 0; u < S; u++) {
+      if constexpr (XREG)
+        consume_step_x<FMT>(raw[u], xr[u], acc);
+      else
+        consume_step<FMT>(raw[u], (uint32_t)u, lane, xs, acc);
+    }
     float a[8];
     acc_unpack(acc, a);
     const float v = tree_butterfly(a, lane);
@@ -420,6 +446,10 @@ __global__ void __launch_bounds__(kGemvThreads, 3) gemv_fixed_kernel(const float
   stage_input(x, N, xs, N);
   __syncthreads();
   g4a::pdl_launch_dependents();
+  if constexpr (XREG) {
+#pragma unroll
+    for (int u = 0; u < S; u++) load_x_pairs(xs, (uint32_t)u, lane, xr[u]);
+  }
   if constexpr (FMT != G4A_WEIGHT_F16) {
     for (; r < jobs.rows; r += stride) {
       StepRaw<FMT> cur[S];
@@ -543,7 +573,19 @@ g4a_status g4a_matmul_group(g4a_ctx* ctx, uint32_t weight_format, const float* i
            gemv_fixed_kernel<G4A_WEIGHT_Q4K, 3>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 4>,
            gemv_fixed_kernel<G4A_WEIGHT_Q4K, 5>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 6>,
            gemv_fixed_kernel<G4A_WEIGHT_Q4K, 7>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 8>}};
-      e = g4a_launch(fixed[weight_format][S - 1], grid, dim3(kGemvThreads), smem, ctx->stream, true, input, J);
+      static const FixedKernel fixed_xreg[2][8] = {
+          {gemv_fixed_kernel<G4A_WEIGHT_Q8, 1, true>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 2, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 3, true>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 4, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 5, true>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 6, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q8, 7, true>, gemv_fixed_kernel<G4A_WEIGHT_Q8, 8, true>},
+          {gemv_fixed_kernel<G4A_WEIGHT_Q4K, 1, true>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 2, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 3, true>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 4, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 5, true>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 6, true>,
+           gemv_fixed_kernel<G4A_WEIGHT_Q4K, 7, true>, gemv_fixed_kernel<G4A_WEIGHT_Q4K, 8, true>}};
+      // streaming-sized row counts: the register-resident input (see gemv_fixed_kernel)
+      const bool xreg = weight_format != G4A_WEIGHT_F16 && rows >= 65536u;
+      e = g4a_launch(xreg ? fixed_xreg[weight_format - 1][S - 1] : fixed[weight_format][S - 1], grid,
+                     dim3(kGemvThreads), smem, ctx->stream, true, input, J);
     } else {
       auto kern = weight_format == G4A_WEIGHT_F16 ? gemv_kernel<G4A_WEIGHT_F16>
                   : weight_format == G4A_WEIGHT_Q8 ? gemv_kernel<G4A_WEIGHT_Q8>

@@ -80,6 +80,15 @@ def test_matmul_long_grid_stride_and_large_n(ctx, oracle):
         ctx.matmul(fmt, dev(x), wd, sd, out, M=M, N=N)
         ctx.sync()
         assert same_bits(host(out), oracle.matmul(fmt, x, wq, sc, M, N))
+    # streaming-sized row counts take the register-resident input variant (Q8 and 4-bit)
+    M, N = 70000, 1536
+    x, w = _inputs(13, M, N)
+    for fmt in (Q8, Q4K):
+        wd, sd, wq, sc = _pack(fmt, w)
+        out = torch.empty((M,), device="cuda")
+        ctx.matmul(fmt, dev(x), wd, sd, out, M=M, N=N)
+        ctx.sync()
+        assert same_bits(host(out), oracle.matmul(fmt, x, wq, sc, M, N)), fmt
     M, N = 64, 12288  # the widest reference matmul input (FFN down of the double-wide layers)
     x, w = _inputs(12, M, N)
     for fmt in (F16, Q8, Q4K):
