@@ -774,7 +774,7 @@ def run_prefill(ctx, torch):
         us = e0.elapsed_time(e1) * 1e3 / n
         fl = synth.prefill_flops(T, W, hd=H5)
         res[name] = {"attn_us": us, "tflops": fl / (us * 1e-6) / 1e12, "frac_of_peak": fl / (us * 1e-6) / 1e12 / bf16,
-                     "flops": fl, "kernel": "prefill_wide_kernel (mma.sync m16n8k16)"}
+                     "flops": fl, "kernel": "prefill_attn_kernel<256, pair> (tcgen05, 2-CTA clusters)"}
     return res
 
 

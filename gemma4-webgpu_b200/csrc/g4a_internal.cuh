@@ -91,9 +91,6 @@ g4a_status g4a_ensure_workspace(g4a_ctx* ctx, size_t bytes);
 g4a_status g4a_dist_check(g4a_ctx* ctx, bool deadline_passed, uint32_t timeout_ms);
 void g4a_dist_release(g4a_ctx* ctx);
 // Prefill through the decode kernels (shapes the tensor-core prefill kernel does not cover).
-// head_dim 512 prefill with 8 q heads per kv head (g4a_prefill_wide.cu).
-g4a_status prefill_wide(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
-                        uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, float scale, uint32_t window);
 g4a_status prefill_via_decode(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
                               uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, uint32_t hd, float scale,
                               uint32_t window);

@@ -38,9 +38,29 @@
 // Every mbarrier wait is bounded; after a timeout the CTA records an error, stops waiting and
 // frees its TMEM.  Barriers that complete once per block come in pairs (one per block parity)
 // wherever a consumer could otherwise fall two phases behind its producer.
+//
+// Head dim 512 (Gemma's global layers), the PAIR instance: one CTA cannot hold a 128-row tile
+// (the f32 O accumulator alone would fill the 512 TMEM columns, the f16 Q tile 128 KB of shared
+// memory), so a cluster of two CTAs computes each tile and CTA c owns head dims [256 c, 256 c +
+// 256): its columns of Q, its halves of every K and V block, its 256 columns of O.  Each CTA
+// computes the partial scores of its dims, S_c = Q_c K_c^T; the two exchange them through
+// distributed shared memory and both add own + partner's (IEEE addition commutes, so the two
+// sums are bit-identical), run the same softmax on the same scores -- hence the same P, running
+// max and l -- and accumulate O_c += P V_c.  No MMA work is duplicated, only the softmax.
+// TMEM (512 columns): O [0, 256), two S buffers [256, 384) with block j's P written over the
+// first 32 columns of its own S buffer (so S_{j+2} is issued after PV_j), and Q [384, 512)
+// (the A operand of the score MMA, written from q16 by the softmax warps).  Shared memory: the
+// 2-stage K and V rings (64 keys x 256 dims) and two slots for the partner's partial scores.
+// Warps 16-19 (640 threads) exchange the partial scores of their TMEM lane quarter: load S_c
+// from TMEM, store it into the partner's slot, arrive on the partner's barrier (release at
+// cluster scope), wait for the partner's (acquire at cluster scope), add, and store the sum
+// into TMEM for the softmax warps.  Every wait is bounded, and a CTA that gives up also sets its
+// partner's abort flag; the two CTAs leave through one cluster barrier, so neither's shared
+// memory goes away while the other may still write to it.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "g4a_internal.cuh"
 
@@ -56,30 +76,38 @@ constexpr float kLog2eP = 1.4426950408889634f;
 constexpr float kRescaleP = 15.0f;         // lazy rescale threshold (log2 units): P <= 2^15 stays in f16 range
 constexpr float kHeadroomP = 8.0f;         // a raised running max is set this far above the block max
 
-template <int HD>
+// HD = head dims held by one CTA (the pair instance: 256 of 512).
+template <int HD, bool PAIR>
 struct PCfg {
+  static constexpr int THREADS = PAIR ? kThreadsP + 128 : kThreadsP;
   static constexpr int NCB = HD / 64;               // 64-dim chunks (128-byte swizzle rows)
   static constexpr int Q_CHUNK = kRows * 128;       // bytes of one chunk of the Q tile
   static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
-  static constexpr int Q_BYTES = NCB * Q_CHUNK;
+  static constexpr int Q_BYTES = PAIR ? 0 : NCB * Q_CHUNK;   // a pair keeps Q in TMEM
   static constexpr int KV_BYTES = NCB * KV_CHUNK;
+  static constexpr int X_BYTES = PAIR ? kRows * kKeys * 4 : 0;  // one slot of the partner's partial scores
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
-  static constexpr int OFF_LSUM = OFF_V + kStagesP * KV_BYTES;  // [2 halves][128 rows] row sums (epilogue)
+  static constexpr int OFF_X = OFF_V + kStagesP * KV_BYTES;     // [2 slots][4 quarters][16][32 lanes][4 floats]
+  static constexpr int OFF_LSUM = OFF_X + 2 * X_BYTES;          // [2 halves][128 rows] row sums (epilogue)
   static constexpr int OFF_RED = OFF_LSUM + 2 * kRows * 4;      // [2 parities][2 halves][128 rows] row maxima
   static constexpr int OFF_ALPHA = OFF_RED + 2 * 2 * kRows * 4; // [2 parities][128 rows] rescale factors
   static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
   static constexpr int OFF_BAR = OFF_FLAG + 64;
-  static constexpr int NBARS = 40;
+  static constexpr int NBARS = 56;
   static constexpr size_t SMEM = 1024 + (size_t)OFF_BAR + NBARS * 8 + 16;
-  // TMEM columns (32-bit each; P holds two f16 per column)
+  // TMEM columns (32-bit each; P and Q hold two f16 per column)
   static constexpr uint32_t COL_O = 0;
   static constexpr uint32_t COL_S = HD;                          // S[b] at COL_S + 64 b
-  static constexpr uint32_t COL_P = COL_S + 2 * kKeys;           // P[b] at COL_P + 32 b
-  static constexpr uint32_t TMEM_COLS = (COL_P + kKeys) <= 256 ? 256u : 512u;
+  // P[b] at COL_P + P_STRIDE b: its own columns, or (pair) over the first half of S[b]
+  static constexpr uint32_t COL_P = PAIR ? COL_S : COL_S + 2 * kKeys;
+  static constexpr uint32_t P_STRIDE = PAIR ? kKeys : kKeys / 2;
+  static constexpr uint32_t COL_Q = COL_S + 2 * kKeys;           // pair: the Q tile (HD / 2 columns)
+  static constexpr uint32_t COL_END = PAIR ? COL_Q + HD / 2 : COL_P + kKeys;
+  static constexpr uint32_t TMEM_COLS = COL_END <= 256 ? 256u : 512u;
   static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte aligned operands");
-  static_assert(COL_P + kKeys <= TMEM_COLS, "TMEM budget");
+  static_assert(COL_END <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -92,6 +120,7 @@ struct PrefillParams {
   float scale_log2;      // scale * log2(e)
   uint32_t window;       // 0 = causal over the whole prefix
   int* err;
+  const uint16_t* q16;   // pair: [T, nqh, 2 HD] f16 queries (read into TMEM)
 };
 
 // --------------------------------------------------------------------------- tcgen05 helpers
@@ -228,13 +257,71 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, wait_or_abort(bar, parity, abort_flag, err, G4A_DEVERR_WAIT_MMA));
 }
 
+// ------------------------------------------------------------------ cluster (CTA pair) helpers
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// Every thread of both CTAs: release this CTA's prior writes, acquire the partner's.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+// Arrive on a barrier of the partner CTA; release at cluster scope orders this thread's prior
+// stores into the partner's shared memory before the arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(g4a::smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the partner's arrivals (acquire at cluster scope), warp-uniform.
+__device__ __forceinline__ bool warp_wait_peer(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  bool done = mbar_try_wait_cluster(bar, parity);
+  if (!done && !*abort_flag) {
+    const uint64_t t0 = g4a::globaltimer_ns();
+    uint32_t spins = 0;
+    while (!(done = mbar_try_wait_cluster(bar, parity))) {
+      if ((++spins & 63u) == 0u) {
+        if (*abort_flag) break;
+        if (g4a::globaltimer_ns() - t0 > 2000000000ull) {
+          *abort_flag = 1;
+          if (err) atomicExch(err, G4A_DEVERR_WAIT_PEER);
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, done);
+}
+
 // --------------------------------------------------------------------------- the kernel
-template <int HD>
-__global__ void __launch_bounds__(kThreadsP, 1)
+template <int HD, bool PAIR>
+__global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmo,
                         const PrefillParams p) {
-  using C = PCfg<HD>;
+  using C = PCfg<HD, PAIR>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -254,12 +341,17 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* barCorr = bars + 21;    // [2] O rescaled for block j (4 correction warps)
   uint64_t* barXchg = bars + 23;    // [2 parities][4 quarters] row-max halves written (2 softmax warps)
   uint64_t* barLsum = bars + 31;    // [4 quarters] row-sum halves written (2 softmax warps)
+  uint64_t* barSx = bars + 35;      // pair: [2 parities][4 quarters] full scores of block j in S[j % 2]
+  uint64_t* barRx = bars + 43;      // pair: [2 slots][4 quarters] partner's partial scores landed (32 lanes)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = (int)(blockIdx.x % (unsigned)p.nkh);
-  const int t0 = (p.ntiles - 1 - (int)(blockIdx.x / (unsigned)p.nkh)) * kTokPerTile;
+  // pair: both CTAs of a cluster take the same tile; cr is this CTA's half of the head dims
+  const uint32_t cr = PAIR ? cluster_ctarank() : 0u;
+  const unsigned tile = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+  const int kvh = (int)(tile % (unsigned)p.nkh);
+  const int t0 = (p.ntiles - 1 - (int)(tile / (unsigned)p.nkh)) * kTokPerTile;
   const int t_last = min(t0 + kTokPerTile, p.T) - 1;
   const uint32_t hi_max = p.start_pos + (uint32_t)t_last + 1u;
   const uint32_t first_hi = p.start_pos + (uint32_t)t0 + 1u;
@@ -282,12 +374,18 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       for (int q = 0; q < 4; q++) g4a::mbar_init(&barXchg[s * 4 + q], 2);
     }
     for (int q = 0; q < 4; q++) g4a::mbar_init(&barLsum[q], 2);
-    g4a::mbar_init(barQ, 1);
+    if (PAIR) {
+      for (int i = 0; i < 8; i++) {
+        g4a::mbar_init(&barSx[i], 1);
+        g4a::mbar_init(&barRx[i], 32);
+      }
+    }
+    g4a::mbar_init(barQ, PAIR ? 8 : 1);  // pair: the 8 softmax warps write Q into TMEM
     g4a::mbar_init(barEnd, 1);
     g4a::mbar_init(barEnd2, 1);
     *abort_flag = 0;
     g4a::fence_mbar_init();
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
+    if (!PAIR) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmo)) : "memory");
@@ -301,7 +399,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   }
   __syncwarp();  // warp 0 was diverged by the initialisation above
   tc_fence_before();
-  __syncthreads();
+  // pair: the partner's barriers are initialised before anyone arrives on them remotely
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   g4a::pdl_launch_dependents();
@@ -315,7 +414,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       const bool kside = warp == 0;
       uint64_t pol_kv;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_kv));
-      if (kside) {
+      if (kside && !PAIR) {
         uint64_t pol_q;
         asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_q));
         g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_BYTES);
@@ -331,12 +430,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                                      G4A_DEVERR_WAIT_EMPTY))
           break;
         g4a::mbar_arrive_expect_tx(&full[s], (uint32_t)C::KV_BYTES);
-        tma_load_4d_p(dst0 + s * C::KV_BYTES, map, 0, kvh, (kb0 + j) * kKeys, 0, &full[s], pol_kv);
+        // pair: this CTA's 64-dim chunks [NCB cr, NCB cr + NCB) of the block
+        tma_load_4d_p(dst0 + s * C::KV_BYTES, map, 0, kvh, (kb0 + j) * kKeys, (int)cr * C::NCB, &full[s], pol_kv);
       }
       // Loads still in flight land before the CTA retires (bounded).
       for (int j = max(0, nb - 2); j < nb; j++)
         (void)wait_or_abort(&full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
-      if (kside) (void)wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+      if (kside && !PAIR) (void)wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------ MMA issuers
@@ -353,9 +453,9 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
         for (int j = 0; ok && j < nb; j++) {
           const int b = j & 1;
-          // S[b] was last read out by the softmax of block j-2
-          if (j >= 2 && !wait_or_abort(&barSfree[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
-                                       G4A_DEVERR_WAIT_MMA))
+          // S[b] was last read out by the softmax of block j-2 (pair: and held P_{j-2} until PV_{j-2})
+          if (j >= 2 && !wait_or_abort(PAIR ? &barPV[b] : &barSfree[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag,
+                                       p.err, G4A_DEVERR_WAIT_MMA))
             break;
           if (!wait_or_abort(&fullK[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
           tc_fence_after();
@@ -364,8 +464,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           for (int kk = 0; kk < HD / 16; kk++) {
             // K step kk: 64-dim chunk kk / 4, 32 bytes (16 dims) per step along the swizzled row
             const uint64_t off = (uint64_t)(((kk & 3) * 32) >> 4);
-            umma_f16_ss(tmem + C::COL_S + (uint32_t)(b * kKeys), dq + (uint64_t)(((kk >> 2) * C::Q_CHUNK) >> 4) + off,
-                        dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK) >> 4) + off, idesc_s, kk > 0 ? 1u : 0u);
+            if constexpr (PAIR)  // Q columns 8 kk .. 8 kk + 7 (two dims per column) in TMEM
+              umma_f16_ts(tmem + C::COL_S + (uint32_t)(b * kKeys), tmem + C::COL_Q + (uint32_t)(kk * 8),
+                          dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK) >> 4) + off, idesc_s, kk > 0 ? 1u : 0u);
+            else
+              umma_f16_ss(tmem + C::COL_S + (uint32_t)(b * kKeys),
+                          dq + (uint64_t)(((kk >> 2) * C::Q_CHUNK) >> 4) + off,
+                          dk + (uint64_t)(((kk >> 2) * C::KV_CHUNK) >> 4) + off, idesc_s, kk > 0 ? 1u : 0u);
           }
           umma_commit(&barS[b]);
           umma_commit(&emptyK[b]);
@@ -385,7 +490,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
           const uint64_t dv = dv0 + (uint64_t)((b * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; kk++) {
-            const uint32_t a = tmem + C::COL_P + (uint32_t)(b * (kKeys / 2) + kk * 8);  // 16 keys = 8 columns
+            const uint32_t a = tmem + C::COL_P + (uint32_t)(b * C::P_STRIDE + kk * 8);  // 16 keys = 8 columns
             umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&barPV[b]);
@@ -409,19 +514,46 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     float* alpha_buf = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
     int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
     const float c2 = p.scale_log2;
+    if constexpr (PAIR) {
+      // The Q tile into TMEM: row r = token t0 + r / 8, head kvh * 8 + r % 8; this CTA's head
+      // dims [HD cr, HD cr + HD), of which this half of the row's threads writes HD / 2.
+      const int qhead = kvh * kHeadsPerKv + r % kHeadsPerKv;
+      const uint4* src =
+          (tok < p.T) ? reinterpret_cast<const uint4*>(p.q16 + ((size_t)tok * p.nqh + qhead) * (2 * HD) + cr * HD +
+                                                       half * (HD / 2))
+                      : nullptr;
+#pragma unroll
+      for (int c = 0; c < HD / 128; c++) {  // 64 dims = 32 columns per store
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const uint4 v = src ? __ldg(src + 8 * c + i) : make_uint4(0u, 0u, 0u, 0u);
+          w[4 * i] = v.x;
+          w[4 * i + 1] = v.y;
+          w[4 * i + 2] = v.z;
+          w[4 * i + 3] = v.w;
+        }
+        tmem_st32(tmem + lane_addr + C::COL_Q + (uint32_t)(half * (HD / 4) + 32 * c), w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(barQ);
+    }
     float m = -INFINITY;
     float lsum = 0.f;  // this half's share of the row sum, relative to m
     bool ok = true;
     for (int j = 0; j < nb; j++) {
       const int b = j & 1;
-      ok = warp_wait(&barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      // pair: the full scores (own + partner's partial) from the exchange warp of this quarter
+      ok = warp_wait(PAIR ? &barSx[b * 4 + quarter] : &barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       tc_fence_after();
       uint32_t sv[32];
       tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys + 32 * half), sv);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(&barSfree[b]);  // S[b] may be overwritten now
+      if (!PAIR && lane == 0) g4a::mbar_arrive(&barSfree[b]);  // S[b] may be overwritten now
       const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys + 32u * half;
       // Interior blocks (every key visible to every row of the warp) skip the mask.
       const bool interior = __all_sync(0xffffffffu, key0 >= lo && key0 + 32u <= hi) && c2 > 0.f;
@@ -458,6 +590,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       ok = warp_wait(&barXchg[b * 4 + quarter], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * kRows + r]);
+      // pair: the other half has loaded its scores (before it arrived), so P may overwrite them
+      if (PAIR) tc_fence_after();
       // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx + kHeadroomP : m;
@@ -508,13 +642,13 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         }
         lsum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       }
-      // P[b] was read by PV_{j-2}
-      if (j >= 2) {
+      // P[b] was read by PV_{j-2} (pair: S_j itself was issued after PV_{j-2})
+      if (!PAIR && j >= 2) {
         ok = warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
         if (!ok) break;
         tc_fence_after();
       }
-      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(b * (kKeys / 2) + 16 * half), pw);
+      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(b * C::P_STRIDE + 16 * half), pw);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -560,11 +694,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     if (warp == 4 && lane == 0 && ok) {
 #pragma unroll 1
       for (int chunk = 0; chunk < HD / 32; chunk++)
-        tma_store_3d(&tmo, obox + (uint32_t)chunk * (kRows * 128), chunk * 32, kvh * kHeadsPerKv, t0);
+        tma_store_3d(&tmo, obox + (uint32_t)chunk * (kRows * 128), chunk * 32 + (int)cr * HD, kvh * kHeadsPerKv, t0);
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // shared memory read before exit
     }
-  } else if (warp >= 12) {
+  } else if (warp < 16) {
     // ------------------------------------------------------------------ O correction
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -605,13 +739,70 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       __syncwarp();
       if (lane == 0) g4a::mbar_arrive(&barCorr[b]);
     }
+  } else if (PAIR) {
+    // ------------------------------------------------------------------ score exchange (pair)
+    // Warp 16 + q: rows 32 q .. 32 q + 31 (TMEM lane quarter q), all 64 keys of a block.  A slot
+    // holds [4 quarters][16 four-key groups][32 lanes][4 floats], so a warp's 16-byte stores and
+    // loads cover 512 consecutive bytes.  Slot b of the partner is written again (block j+2) only
+    // after the partner's block j+1 scores arrived here, which it sent after reading slot b.
+    const int quarter = warp & 3;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t peer = cr ^ 1u;
+    const uint32_t xoff = C::OFF_X + (uint32_t)quarter * (16 * 32 * 16) + (uint32_t)lane * 16;
+    const uint32_t x_peer = mapa_shared(sbase, peer) + xoff;
+    const uint32_t rx_peer = mapa_shared(g4a::smem_u32(barRx), peer);
+    bool ok = true;
+    for (int j = 0; j < nb; j++) {
+      const int b = j & 1;
+      ok = warp_wait(&barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t slot = (uint32_t)b * C::X_BYTES;
+      const uint32_t scol = tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys);
+#pragma unroll 1
+      for (int h = 0; h < 2; h++) {  // 32 keys at a time (registers)
+        uint32_t own[32];
+        tmem_ld32(scol + 32u * h, own);
+#pragma unroll
+        for (int g = 0; g < 8; g++)
+          st_cluster_v4(x_peer + slot + (8 * h + g) * 512, own[4 * g], own[4 * g + 1], own[4 * g + 2], own[4 * g + 3]);
+      }
+      mbar_arrive_remote(rx_peer + (uint32_t)(b * 4 + quarter) * 8u);
+      ok = warp_wait_peer(&barRx[b * 4 + quarter], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      if (!ok) break;
+      const unsigned char* xs = smem + xoff + slot;
+#pragma unroll 1
+      for (int h = 0; h < 2; h++) {  // own partial again from TMEM, + the partner's, back into TMEM
+        uint32_t own[32];
+        tmem_ld32(scol + 32u * h, own);
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+          const float4 v = *reinterpret_cast<const float4*>(xs + (8 * h + g) * 512);
+          own[4 * g] = __float_as_uint(__uint_as_float(own[4 * g]) + v.x);
+          own[4 * g + 1] = __float_as_uint(__uint_as_float(own[4 * g + 1]) + v.y);
+          own[4 * g + 2] = __float_as_uint(__uint_as_float(own[4 * g + 2]) + v.z);
+          own[4 * g + 3] = __float_as_uint(__uint_as_float(own[4 * g + 3]) + v.w);
+        }
+        tmem_st32(scol + 32u * h, own);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) g4a::mbar_arrive(&barSx[b * 4 + quarter]);
+    }
+    // A CTA that gave up stops its partner's waits too (the partner is still resident: it
+    // leaves only through the cluster barrier below).
+    if (!ok && lane == 0) {
+      const uint32_t peer_abort = mapa_shared(g4a::smem_u32((const void*)abort_flag), peer);
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
+    }
   }
   // The single-lane roles above leave their warps diverged: reconverge every warp before the
   // CTA barrier, so that it waits for each lane (an aligned barrier reached by part of a warp
   // is not a barrier for the rest of it).
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS) : "memory");
@@ -632,8 +823,8 @@ g4a_status get_encoder_p(g4a_ctx* ctx, PFN_cuTensorMapEncodeTiled_v12000* out) {
 }
 
 // {64, heads, rows, chunks} f16 map with the chunk index outermost (stride 128 B), 128-byte
-// swizzle, box {64, box_heads, box_rows, chunks}: one TMA op lands a tile as `chunks` column
-// boxes of [box_heads * box_rows rows x 128 B].
+// swizzle, box {64, box_heads, box_rows, box_chunks}: one TMA op lands a tile as `box_chunks`
+// column boxes of [box_heads * box_rows rows x 128 B].
 // The f32 output [T, nqh, HD] as {HD, nqh, T} with 128-byte swizzle and box {32, 8, 16}: one
 // TMA store writes 32 columns of a tile's 16 tokens x 8 heads; rows past T are not written.
 g4a_status encode_out_map(g4a_ctx* ctx, CUtensorMap* map, float* base, uint32_t hd, uint32_t nqh, uint32_t T) {
@@ -650,13 +841,14 @@ g4a_status encode_out_map(g4a_ctx* ctx, CUtensorMap* map, float* base, uint32_t 
 }
 
 g4a_status encode_rows_map(g4a_ctx* ctx, CUtensorMap* map, const void* base, uint32_t hd, uint32_t heads,
-                           uint64_t rows, uint32_t box_heads, uint32_t box_rows, const char* what) {
+                           uint64_t rows, uint32_t box_heads, uint32_t box_rows, uint32_t box_chunks,
+                           const char* what) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   if (g4a_status s = get_encoder_p(ctx, &enc)) return s;
   const cuuint64_t ncb = hd / 64;
   cuuint64_t dims[4] = {64, heads, rows, ncb};
   cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)heads * hd * 2, 128};
-  cuuint32_t box[4] = {64, box_heads, box_rows, (cuuint32_t)ncb};
+  cuuint32_t box[4] = {64, box_heads, box_rows, box_chunks};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -665,22 +857,29 @@ g4a_status encode_rows_map(g4a_ctx* ctx, CUtensorMap* map, const void* base, uin
   return G4A_OK;
 }
 
+// HD = head dims of the layer; the pair instance (HD 512) gives each CTA of a cluster 256.
 template <int HD>
 g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, const uint16_t* v, float* out,
                           uint32_t T, uint32_t start_pos, uint32_t nqh, uint32_t nkh, float scale, uint32_t window) {
-  using C = PCfg<HD>;
-  static bool configured[64] = {false};
-  if (ctx->device >= 64 || !configured[ctx->device]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  constexpr bool kPair = HD == 512;
+  constexpr int kHdCta = kPair ? HD / 2 : HD;
+  using C = PCfg<kHdCta, kPair>;
+  auto kernel = prefill_attn_kernel<kHdCta, kPair>;
+  static std::atomic<bool> configured[64];
+  if (ctx->device >= 64 || !configured[ctx->device].load()) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return g4a_cuda_fail(e, "cudaFuncSetAttribute(prefill_attn_kernel)");
-    if (ctx->device < 64) configured[ctx->device] = true;
+    if (ctx->device < 64) configured[ctx->device].store(true);
   }
   CUtensorMap mq, mk, mv;
-  if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, "q16")) return s;
   const uint64_t rows = (uint64_t)start_pos + T;
-  if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, "the K cache")) return s;
-  if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, "the V cache")) return s;
+  // pair: each CTA loads its NCB of the HD / 64 chunks of a K or V block (Q is read into TMEM)
+  if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, C::NCB, "the K cache")) return s;
+  if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, C::NCB, "the V cache")) return s;
+  if (kPair)
+    mq = mk;  // unused
+  else if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, C::NCB, "q16"))
+    return s;
   CUtensorMap mo;
   if (g4a_status s = encode_out_map(ctx, &mo, out, HD, nqh, T)) return s;
   PrefillParams p = {};
@@ -693,9 +892,23 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   p.scale_log2 = scale * kLog2eP;
   p.window = window;
   p.err = ctx->dev_err_dev;
+  p.q16 = q16;
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
-  cudaError_t e = g4a_launch(prefill_attn_kernel<HD>, dim3((unsigned)(p.ntiles * p.nkh)), dim3(kThreadsP), C::SMEM,
-                             ctx->stream, true, mq, mk, mv, mo, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.ntiles * p.nkh * (kPair ? 2 : 1)));
+  cfg.blockDim = dim3((unsigned)C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // pair: the two CTAs of a tile
+  attr[1].val.clusterDim.x = kPair ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kPair ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mq, mk, mv, mo, p);
   if (e != cudaSuccess) return g4a_cuda_fail(e, "launch prefill_attn_kernel");
   return G4A_OK;
 }
@@ -716,15 +929,14 @@ extern "C" g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const 
     return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: pointers must be 16-byte aligned");
   if ((uint64_t)start_pos + T > 0xffffffffull) return g4a_fail(G4A_EINVAL, "g4a_prefill_attn: start_pos + T overflows");
   if (T == 0) return G4A_OK;
-  // The tcgen05 kernel covers GQA 8:1 at head_dim 128 and 256, the warp-MMA kernel of
-  // g4a_prefill_wide.cu GQA 8:1 at head_dim 512 (Gemma's global layers); every other shape runs
-  // through the decode kernels.
-  if (num_q_heads == (uint32_t)kHeadsPerKv * num_kv_heads && head_dim == 512)
-    return prefill_wide(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
-                        sliding_window);
-  if (num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads || (head_dim != 128 && head_dim != 256))
+  // The tcgen05 kernel covers GQA 8:1 at head_dim 128 and 256, and at head_dim 512 (Gemma's
+  // global layers) as CTA pairs; every other shape runs through the decode kernels.
+  if (num_q_heads != (uint32_t)kHeadsPerKv * num_kv_heads || (head_dim != 128 && head_dim != 256 && head_dim != 512))
     return prefill_via_decode(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, head_dim,
                               scale, sliding_window);
+  if (head_dim == 512)
+    return launch_prefill<512>(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
+                               sliding_window);
   if (head_dim == 256)
     return launch_prefill<256>(ctx, q16, k_cache, v_cache, out, T, start_pos, num_q_heads, num_kv_heads, scale,
                                sliding_window);

@@ -128,17 +128,19 @@ def test_prefill_repeatable(ctx):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-# head_dim 512 with GQA 8:1 (Gemma's global layers) runs on the warp-MMA kernel of
-# g4a_prefill_wide.cu; other shapes run through the decode kernels (the fast decode path for
-# head_dim 512 with other ratios is not used; GQA 4:1 and 3:1 take the generic kernel).
+# head_dim 512 with GQA 8:1 (Gemma's global layers) runs on the tensor-core kernel as CTA pairs
+# (each CTA of a cluster owns 256 of the 512 dims and the two exchange partial scores); other
+# shapes run through the decode kernels (the fast decode path for head_dim 512 with other ratios
+# is not used; GQA 4:1 and 3:1 take the generic kernel).
 FALLBACK = [
     (70, 0, 0, 512, 1, 8),      # Gemma global layer: head_dim 512, causal
     (90, 300, 512, 512, 1, 8),  # head_dim 512, sliding, after a prefix
     (1, 0, 0, 512, 1, 8),       # one token
     (7, 0, 0, 512, 1, 8),       # a partial tile
-    (8, 0, 0, 512, 1, 8),       # exactly one tile
-    (9, 3, 0, 512, 1, 8),       # one row past a tile, after a prefix
-    (257, 40, 33, 512, 2, 16),  # two kv heads, window not a multiple of the 32-key block
+    (16, 0, 0, 512, 1, 8),      # exactly one tile (16 tokens x 8 heads)
+    (17, 3, 0, 512, 1, 8),      # one row past a tile, after a prefix
+    (257, 40, 33, 512, 2, 16),  # two kv heads (two tiles per token group), window not a multiple of 64
+    (200, 0, 64, 512, 1, 8),    # window of exactly one key block
     (130, 1000, 64, 512, 1, 8), # long prefix, small window
     (33, 5, 0, 256, 1, 4),      # GQA 4:1 (generic kernel)
     (48, 0, 16, 64, 2, 6),      # GQA 3:1, small head_dim, tiny window
@@ -177,7 +179,7 @@ def test_prefill_head_dim_512_full_size(ctx, oracle, W, theta):
     assert np.array_equal(host(out).view(np.uint32), host(again).view(np.uint32))
     ref = _torch_ref(q16, kc, vc, 0, W, rows_per_chunk=128)
     assert_attention_close(host(out), host(ref), what=f"hd512 W={W} vs torch fp32")
-    rows = [0, 1, 7, 8, 9, 31, 32, 33, 511, 512, 513, 2047, 4088, 4095]
+    rows = [0, 1, 7, 8, 9, 15, 16, 17, 31, 32, 33, 63, 64, 65, 511, 512, 513, 2047, 4080, 4088, 4095]
     ref64 = oracle.prefill_rows_f64(host(q16).astype(np.float32), host(kc), host(vc), rows, start_pos=0,
                                     num_q_heads=8, num_kv_heads=1, head_dim=512, sliding_window=W)
     assert_attention_close(host(out)[rows], ref64, what=f"hd512 W={W} vs oracle")
