@@ -47,16 +47,19 @@
 // distributed shared memory and both add own + partner's (IEEE addition commutes, so the two
 // sums are bit-identical), run the same softmax on the same scores -- hence the same P, running
 // max and l -- and accumulate O_c += P V_c.  No MMA work is duplicated, only the softmax.
-// TMEM (512 columns): O [0, 256), two S buffers [256, 384) with block j's P written over the
-// first 32 columns of its own S buffer (so S_{j+2} is issued after PV_j), and Q [384, 512)
-// (the A operand of the score MMA, written from q16 by the softmax warps).  Shared memory: the
-// 2-stage K and V rings (64 keys x 256 dims) and two slots for the partner's partial scores.
-// Warps 16-19 (640 threads) exchange the partial scores of their TMEM lane quarter: load S_c
-// from TMEM, store it into the partner's slot, arrive on the partner's barrier (release at
-// cluster scope), wait for the partner's (acquire at cluster scope), add, and store the sum
-// into TMEM for the softmax warps.  Every wait is bounded, and a CTA that gives up also sets its
-// partner's abort flag; the two CTAs leave through one cluster barrier, so neither's shared
-// memory goes away while the other may still write to it.
+// TMEM (512 columns): O [0, 256), two S buffers [256, 384), and Q [384, 512) (the A operand of
+// the score MMA, written from q16 by the softmax warps).  P goes to shared memory (one 16 KB
+// buffer, the A operand of the PV MMA).  Shared memory also holds the 2-stage K and V rings (64
+// keys x 256 dims) and, per TMEM lane quarter, one 8 KB slot for the scores this CTA sends and
+// one for the partner's it receives.  Warps 16-19 (640 threads) exchange the partial scores of
+// their lane quarter: load S_c from TMEM, stage it in shared memory, send it with one bulk copy
+// into the partner's receive slot (completing on the partner's barrier), wait for the
+// partner's, add, and store the sum into TMEM for the softmax warps.  (Per-thread remote stores
+// took 1.5 us per block for the 32 KB, and the exchange inside the softmax warps put it on their
+// critical path.)  A warp stages block j only after the partner has read block j-1 (a remote
+// arrival), which also tells it that its own previous copy has landed.  Every wait is bounded,
+// and a CTA that gives up also sets its partner's abort flag; the two CTAs leave through one
+// cluster barrier, so neither's shared memory goes away while the other may still copy into it.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -85,12 +88,16 @@ struct PCfg {
   static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
   static constexpr int Q_BYTES = PAIR ? 0 : NCB * Q_CHUNK;   // a pair keeps Q in TMEM
   static constexpr int KV_BYTES = NCB * KV_CHUNK;
-  static constexpr int X_BYTES = PAIR ? kRows * kKeys * 4 : 0;  // one slot of the partner's partial scores
+  static constexpr int X_BYTES = PAIR ? kRows * kKeys * 4 : 0;  // one block's partial scores (f32)
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + kStagesP * KV_BYTES;
-  static constexpr int OFF_X = OFF_V + kStagesP * KV_BYTES;     // [2 slots][4 quarters][16][32 lanes][4 floats]
-  static constexpr int OFF_LSUM = OFF_X + 2 * X_BYTES;          // [2 halves][128 rows] row sums (epilogue)
+  // pair: [4 quarters] x 8 KB ([16 four-key groups][32 lanes][4 floats]) of the scores this CTA
+  // sends (OFF_XS) and of the partner's it receives (OFF_XR); P [128 rows][128 B] (OFF_P)
+  static constexpr int OFF_XS = OFF_V + kStagesP * KV_BYTES;
+  static constexpr int OFF_XR = OFF_XS + X_BYTES;
+  static constexpr int OFF_P = OFF_XR + X_BYTES;
+  static constexpr int OFF_LSUM = OFF_P + (PAIR ? kRows * kKeys * 2 : 0);  // [2 halves][128 rows] row sums
   static constexpr int OFF_RED = OFF_LSUM + 2 * kRows * 4;      // [2 parities][2 halves][128 rows] row maxima
   static constexpr int OFF_ALPHA = OFF_RED + 2 * 2 * kRows * 4; // [2 parities][128 rows] rescale factors
   static constexpr int OFF_FLAG = OFF_ALPHA + 2 * kRows * 4;    // [2 parities][4 quarters] rescale needed
@@ -100,13 +107,12 @@ struct PCfg {
   // TMEM columns (32-bit each; P and Q hold two f16 per column)
   static constexpr uint32_t COL_O = 0;
   static constexpr uint32_t COL_S = HD;                          // S[b] at COL_S + 64 b
-  // P[b] at COL_P + P_STRIDE b: its own columns, or (pair) over the first half of S[b]
-  static constexpr uint32_t COL_P = PAIR ? COL_S : COL_S + 2 * kKeys;
-  static constexpr uint32_t P_STRIDE = PAIR ? kKeys : kKeys / 2;
+  static constexpr uint32_t COL_P = COL_S + 2 * kKeys;           // P[b] at COL_P + 32 b (pair: in shared memory)
   static constexpr uint32_t COL_Q = COL_S + 2 * kKeys;           // pair: the Q tile (HD / 2 columns)
   static constexpr uint32_t COL_END = PAIR ? COL_Q + HD / 2 : COL_P + kKeys;
   static constexpr uint32_t TMEM_COLS = COL_END <= 256 ? 256u : 512u;
-  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && KV_BYTES % 1024 == 0, "1024-byte aligned operands");
+  static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && KV_BYTES % 1024 == 0,
+                "1024-byte aligned operands");
   static_assert(COL_END <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -279,10 +285,18 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_
   asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
 }
-// Arrive on a barrier of the partner CTA; release at cluster scope orders this thread's prior
-// stores into the partner's shared memory before the arrival.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+// Arrive on a barrier of the partner CTA, with no ordering of this thread's prior memory
+// operations (the caller has no writes to publish: the arrival only says that a slot was read).
+// Bulk copy of `bytes` from this CTA's shared memory into the partner's (dst and bar are
+// shared::cluster addresses from mapa), completing as transaction bytes on the partner's barrier.
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst),
+               "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -341,14 +355,16 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
   uint64_t* barCorr = bars + 21;    // [2] O rescaled for block j (4 correction warps)
   uint64_t* barXchg = bars + 23;    // [2 parities][4 quarters] row-max halves written (2 softmax warps)
   uint64_t* barLsum = bars + 31;    // [4 quarters] row-sum halves written (2 softmax warps)
-  uint64_t* barSx = bars + 35;      // pair: [2 parities][4 quarters] full scores of block j in S[j % 2]
-  uint64_t* barRx = bars + 43;      // pair: [2 slots][4 quarters] partner's partial scores landed (32 lanes)
+  uint64_t* barRx = bars + 35;      // pair: [4 quarters] the partner's partial scores landed
+  uint64_t* barOK = bars + 39;      // pair: [4 quarters] the partner has read this CTA's
+  uint64_t* barSx = bars + 43;      // pair: [2 parities][4 quarters] the full scores of block j in S[j % 2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // pair: both CTAs of a cluster take the same tile; cr is this CTA's half of the head dims
   const uint32_t cr = PAIR ? cluster_ctarank() : 0u;
+  const uint32_t peer = cr ^ 1u;
   const unsigned tile = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
   const int kvh = (int)(tile % (unsigned)p.nkh);
   const int t0 = (p.ntiles - 1 - (int)(tile / (unsigned)p.nkh)) * kTokPerTile;
@@ -375,10 +391,11 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
     }
     for (int q = 0; q < 4; q++) g4a::mbar_init(&barLsum[q], 2);
     if (PAIR) {
-      for (int i = 0; i < 8; i++) {
-        g4a::mbar_init(&barSx[i], 1);
-        g4a::mbar_init(&barRx[i], 32);
+      for (int i = 0; i < 4; i++) {
+        g4a::mbar_init(&barRx[i], 1);  // the exchange warp's expect_tx + the partner's copy
+        g4a::mbar_init(&barOK[i], 1);  // the partner's exchange warp (remote arrival)
       }
+      for (int i = 0; i < 8; i++) g4a::mbar_init(&barSx[i], 1);
     }
     g4a::mbar_init(barQ, PAIR ? 8 : 1);  // pair: the 8 softmax warps write Q into TMEM
     g4a::mbar_init(barEnd, 1);
@@ -453,9 +470,9 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
         bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
         for (int j = 0; ok && j < nb; j++) {
           const int b = j & 1;
-          // S[b] was last read out by the softmax of block j-2 (pair: and held P_{j-2} until PV_{j-2})
-          if (j >= 2 && !wait_or_abort(PAIR ? &barPV[b] : &barSfree[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag,
-                                       p.err, G4A_DEVERR_WAIT_MMA))
+          // S[b] was last read out by the softmax of block j-2
+          if (j >= 2 && !wait_or_abort(&barSfree[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err,
+                                       G4A_DEVERR_WAIT_MMA))
             break;
           if (!wait_or_abort(&fullK[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
           tc_fence_after();
@@ -480,6 +497,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
         // V block as the MN-major B operand: 64 dims per 128-byte row (N), chunks C::KV_CHUNK apart
         // (leading offset), 8-key row groups 1024 bytes apart (stride offset).
         const uint64_t dv0 = sw128_desc(sbase + C::OFF_V, (uint32_t)C::KV_CHUNK, 1024);
+        const uint64_t dp = sw128_desc(sbase + C::OFF_P, 16, 1024);  // pair: P [128 rows][64 keys], K-major
         for (int i = 0; i < nb; i++) {
           const int b = i & 1;
           if (!wait_or_abort(&fullV[b], (uint32_t)(i >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL)) break;
@@ -490,8 +508,14 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
           const uint64_t dv = dv0 + (uint64_t)((b * C::KV_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < kKeys / 16; kk++) {
-            const uint32_t a = tmem + C::COL_P + (uint32_t)(b * C::P_STRIDE + kk * 8);  // 16 keys = 8 columns
-            umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR) {  // 16 keys = 32 bytes along P's swizzled rows
+              umma_f16_ss(tmem + C::COL_O, dp + (uint64_t)((kk * 32) >> 4), dv + (uint64_t)((kk * 2048) >> 4), idesc_pv,
+                          (i > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint32_t a = tmem + C::COL_P + (uint32_t)(b * (kKeys / 2) + kk * 8);  // 16 keys = 8 columns
+              umma_f16_ts(tmem + C::COL_O, a, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv,
+                          (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&barPV[b]);
           umma_commit(&emptyV[b]);
@@ -553,7 +577,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       tmem_ld32(tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys + 32 * half), sv);
       tc_fence_before();
       __syncwarp();
-      if (!PAIR && lane == 0) g4a::mbar_arrive(&barSfree[b]);  // S[b] may be overwritten now
+      if (lane == 0) g4a::mbar_arrive(&barSfree[b]);  // S[b] may be overwritten now
       const uint32_t key0 = (uint32_t)(kb0 + j) * kKeys + 32u * half;
       // Interior blocks (every key visible to every row of the warp) skip the mask.
       const bool interior = __all_sync(0xffffffffu, key0 >= lo && key0 + 32u <= hi) && c2 > 0.f;
@@ -590,8 +614,6 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       ok = warp_wait(&barXchg[b * 4 + quarter], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       mx = fmaxf(mx, red[(b * 2 + (half ^ 1)) * kRows + r]);
-      // pair: the other half has loaded its scores (before it arrived), so P may overwrite them
-      if (PAIR) tc_fence_after();
       // lazy rescale: the running max is only raised when it grows by more than 2^kRescaleP
       const bool grow = mx > m + kRescaleP;
       const float m_new = grow ? mx + kHeadroomP : m;
@@ -642,18 +664,42 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
         }
         lsum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
       }
-      // P[b] was read by PV_{j-2} (pair: S_j itself was issued after PV_{j-2})
-      if (!PAIR && j >= 2) {
-        ok = warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
-        if (!ok) break;
-        tc_fence_after();
+      if constexpr (PAIR) {
+        // the single P buffer was read by PV_{j-1}
+        if (j >= 1) {
+          ok = warp_wait(&barPV[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, abort_flag, p.err);
+          if (!ok) break;
+        }
+        // row r, keys 32 half .. 32 half + 31 = 16-byte chunks 4 half .. 4 half + 3 of the row's
+        // 128 bytes, chunk c stored at c ^ (r & 7) (the 128-byte swizzle of the MMA descriptor)
+        const uint32_t prow = sbase + C::OFF_P + (uint32_t)r * 128u;
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                           prow + (uint32_t)(((4 * half + cc) ^ (r & 7)) << 4)),
+                       "r"(pw[4 * cc]), "r"(pw[4 * cc + 1]), "r"(pw[4 * cc + 2]), "r"(pw[4 * cc + 3])
+                       : "memory");
+        g4a::fence_proxy_async_smem();  // visible to the tensor core's reads
+      } else {
+        // P[b] was read by PV_{j-2}
+        if (j >= 2) {
+          ok = warp_wait(&barPV[b], (uint32_t)((j >> 1) - 1) & 1u, abort_flag, p.err);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(b * (kKeys / 2) + 16 * half), pw);
+        tmem_wait_st();
+        tc_fence_before();
       }
-      tmem_st16(tmem + lane_addr + C::COL_P + (uint32_t)(b * C::P_STRIDE + 16 * half), pw);
-      tmem_wait_st();
-      tc_fence_before();
       __syncwarp();
       if (lane == 0) g4a::mbar_arrive(&barP[b]);
     }
+    // pair: a warp that gave up stops the partner's waits too (the partner is still resident: it
+    // leaves only through the cluster barrier at the end)
+    if (PAIR && !ok && lane == 0)
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(g4a::smem_u32((const void*)abort_flag), peer)),
+                   "r"(1u)
+                   : "memory");
     // epilogue: l = both halves' sums (added in the same order by both), then O / l, each half
     // of the row's threads storing half of the columns
     float* lsum_buf = reinterpret_cast<float*>(smem + C::OFF_LSUM);  // [half][row]
@@ -698,7 +744,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // shared memory read before exit
     }
-  } else if (warp < 16) {
+  } else if (warp < 16) {  // warps 12-15 (the pair's exchange warps are 16-19)
     // ------------------------------------------------------------------ O correction
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -741,43 +787,55 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
     }
   } else if (PAIR) {
     // ------------------------------------------------------------------ score exchange (pair)
-    // Warp 16 + q: rows 32 q .. 32 q + 31 (TMEM lane quarter q), all 64 keys of a block.  A slot
-    // holds [4 quarters][16 four-key groups][32 lanes][4 floats], so a warp's 16-byte stores and
-    // loads cover 512 consecutive bytes.  Slot b of the partner is written again (block j+2) only
-    // after the partner's block j+1 scores arrived here, which it sent after reading slot b.
+    // Warp 16 + q: rows 32 q .. 32 q + 31 (TMEM lane quarter q), all 64 keys of a block.
     const int quarter = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const uint32_t peer = cr ^ 1u;
-    const uint32_t xoff = C::OFF_X + (uint32_t)quarter * (16 * 32 * 16) + (uint32_t)lane * 16;
-    const uint32_t x_peer = mapa_shared(sbase, peer) + xoff;
-    const uint32_t rx_peer = mapa_shared(g4a::smem_u32(barRx), peer);
+    const uint32_t xs = sbase + C::OFF_XS + (uint32_t)quarter * 8192u;
+    const uint32_t xr = sbase + C::OFF_XR + (uint32_t)quarter * 8192u;
+    const uint32_t xr_peer = mapa_shared(xr, peer);
+    const uint32_t rx_peer = mapa_shared(g4a::smem_u32(&barRx[quarter]), peer);
+    const uint32_t ok_peer = mapa_shared(g4a::smem_u32(&barOK[quarter]), peer);
     bool ok = true;
     for (int j = 0; j < nb; j++) {
       const int b = j & 1;
       ok = warp_wait(&barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t slot = (uint32_t)b * C::X_BYTES;
       const uint32_t scol = tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys);
+      // the partner has read block j-1 from its slot, so the copy from xs has landed
+      if (j >= 1) {
+        ok = warp_wait_peer(&barOK[quarter], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
+        if (!ok) break;
+      }
 #pragma unroll 1
       for (int h = 0; h < 2; h++) {  // 32 keys at a time (registers)
         uint32_t own[32];
         tmem_ld32(scol + 32u * h, own);
 #pragma unroll
         for (int g = 0; g < 8; g++)
-          st_cluster_v4(x_peer + slot + (8 * h + g) * 512, own[4 * g], own[4 * g + 1], own[4 * g + 2], own[4 * g + 3]);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(xs + (uint32_t)((8 * h + g) * 512 + lane * 16)),
+                       "r"(own[4 * g]), "r"(own[4 * g + 1]), "r"(own[4 * g + 2]), "r"(own[4 * g + 3])
+                       : "memory");
       }
-      mbar_arrive_remote(rx_peer + (uint32_t)(b * 4 + quarter) * 8u);
-      ok = warp_wait_peer(&barRx[b * 4 + quarter], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
+      g4a::fence_proxy_async_smem();  // the staged scores are visible to the copy engine
+      __syncwarp();
+      if (lane == 0) {
+        g4a::mbar_arrive_expect_tx(&barRx[quarter], 8192u);  // the partner's block j, into xr
+        bulk_s2s_cluster(xr_peer, xs, 8192u, rx_peer);
+      }
+      ok = warp_wait_peer(&barRx[quarter], (uint32_t)j & 1u, abort_flag, p.err);
       if (!ok) break;
-      const unsigned char* xs = smem + xoff + slot;
 #pragma unroll 1
       for (int h = 0; h < 2; h++) {  // own partial again from TMEM, + the partner's, back into TMEM
         uint32_t own[32];
         tmem_ld32(scol + 32u * h, own);
 #pragma unroll
         for (int g = 0; g < 8; g++) {
-          const float4 v = *reinterpret_cast<const float4*>(xs + (8 * h + g) * 512);
+          float4 v;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                       : "r"(xr + (uint32_t)((8 * h + g) * 512 + lane * 16))
+                       : "memory");
           own[4 * g] = __float_as_uint(__uint_as_float(own[4 * g]) + v.x);
           own[4 * g + 1] = __float_as_uint(__uint_as_float(own[4 * g + 1]) + v.y);
           own[4 * g + 2] = __float_as_uint(__uint_as_float(own[4 * g + 2]) + v.z);
@@ -787,15 +845,16 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(&barSx[b * 4 + quarter]);
+      __syncwarp();  // every lane has read the slot and stored its sums
+      if (lane == 0) {
+        g4a::mbar_arrive(&barSx[b * 4 + quarter]);
+        mbar_arrive_remote_relaxed(ok_peer);  // the slot's values are in registers already
+      }
     }
-    // A CTA that gave up stops its partner's waits too (the partner is still resident: it
-    // leaves only through the cluster barrier below).
-    if (!ok && lane == 0) {
-      const uint32_t peer_abort = mapa_shared(g4a::smem_u32((const void*)abort_flag), peer);
-      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
-    }
+    if (!ok && lane == 0)  // stop the partner's waits too
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(g4a::smem_u32((const void*)abort_flag), peer)),
+                   "r"(1u)
+                   : "memory");
   }
   // The single-lane roles above leave their warps diverged: reconverge every warp before the
   // CTA barrier, so that it waits for each lane (an aligned barrier reached by part of a warp
