@@ -255,9 +255,9 @@ g4a_status g4a_prefill_qkv_prep(g4a_ctx* ctx, const float* q, const float* k, co
  * the cache already holds rows 0 .. start_pos+T-1.  Row i attends to cache positions
  * [max(0, start_pos+i+1-W), start_pos+i] -- exactly decode at kv_len = start_pos+i+1, which is
  * what the reference's token-by-token prefill computes.  out is f32 [T, num_q_heads,
- * head_dim].  num_q_heads/num_kv_heads = 8 at head_dim 128 or 256 runs on the tcgen05 tensor
- * cores, at head_dim 512 (Gemma's global layers) on the warp-level MMA with O in registers;
- * every other shape (head_dim a multiple of 8 up to 512, any num_kv_heads <= num_q_heads)
+ * head_dim].  num_q_heads/num_kv_heads = 8 at head_dim 128, 256 or 512 runs on the tcgen05
+ * tensor cores (at head_dim 512, Gemma's global layers, each tile on a 2-CTA cluster that splits
+ * the head dims); every other shape (head_dim a multiple of 8 up to 512, any num_kv_heads <= num_q_heads)
  * runs through the decode kernels, one decode problem per prompt token, with the same results
  * and several times the run time.  All pointers 16-byte aligned. */
 g4a_status g4a_prefill_attn(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k_cache,
