@@ -60,7 +60,7 @@ def parse():
                     help="small profiling workload: config[3] prefill with sliding window W (0 = causal), "
                          "three launches, no timing")
     ap.add_argument("--ncu-head-dim", type=int, default=256, choices=[128, 256, 512],
-                    help="head_dim of the --ncu-prefill case (512: the warp-MMA kernel of the global layers)")
+                    help="head_dim of the --ncu-prefill case (512: the CTA-pair kernel of the global layers)")
     ap.add_argument("--ncu-matmul", type=int, default=-1, metavar="FMT",
                     help="only run three lm-head sized GEMV launches (262144 x 1536) of weight format FMT "
                          "(0 f16, 1 Q8, 2 4-bit), for an ncu capture")
@@ -494,10 +494,19 @@ def run_e2e(ctx, torch, kcs, vcs, L, R, calls, rank, world=1, dist=None):
     torch.cuda.synchronize()
     ms = _max_over_ranks(torch, dist, e0.elapsed_time(e1))
     assert np.isfinite(hout.numpy()).all()
+    # Host cost of a call on its own: a short burst into an idle stream (in the long run above the
+    # launch queue fills and the host waits for the device, so its time per call is the device's).
+    burst = min(32, calls)
+    b0 = time.perf_counter()
+    for i in range(burst):
+        layer_call(i % R)
+    b1 = time.perf_counter()
+    torch.cuda.synchronize()
     return {"value": kv_bytes(L) * calls * world / (ms / 1e3) / 1e9, "unit": "GB/s",
             "h2d_bytes_per_step": nb(hqkv), "d2h_bytes_per_step": nb(hout),
             "us_per_layer": ms * 1e3 / calls, "layer_calls_per_rank": calls,
-            "host_enqueue_us_per_call": (h1 - h0) * 1e6 / calls,
+            "host_enqueue_us_per_call": (b1 - b0) * 1e6 / burst,
+            "host_us_per_call_in_run": (h1 - h0) * 1e6 / calls,
             "path": "one g4a_attn_decode_layer_io call per layer call: the producer kernel reads q|k|v "
                     "(10,240 B) from pinned host memory over PCIe, the layer runs (q/k norm+RoPE, v_norm, store, "
                     "attention), the attention writes the output (8,192 B) into pinned host memory"}
