@@ -48,7 +48,9 @@
 // sums are bit-identical), run the same softmax on the same scores -- hence the same P, running
 // max and l -- and accumulate O_c += P V_c.  No MMA work is duplicated, only the softmax.
 // TMEM (512 columns): O [0, 256), two S buffers [256, 384), and Q [384, 512) (the A operand of
-// the score MMA, written from q16 by the softmax warps).  P goes to shared memory (one 16 KB
+// the score MMA: one TMA load into the idle send and receive slots, which the exchange warps
+// then copy into TMEM before the first exchange; the partner sends its first scores only after
+// this CTA's exchange warps have read the slots, the same signal as for every later block).  P goes to shared memory (one 16 KB
 // buffer, the A operand of the PV MMA).  Shared memory also holds the 2-stage K and V rings (64
 // keys x 256 dims) and, per TMEM lane quarter, one 8 KB slot for the scores this CTA sends and
 // one for the partner's it receives.  Warps 16-19 (640 threads) exchange the partial scores of
@@ -86,7 +88,8 @@ struct PCfg {
   static constexpr int NCB = HD / 64;               // 64-dim chunks (128-byte swizzle rows)
   static constexpr int Q_CHUNK = kRows * 128;       // bytes of one chunk of the Q tile
   static constexpr int KV_CHUNK = kKeys * 128;      // bytes of one chunk of a K or V block
-  static constexpr int Q_BYTES = PAIR ? 0 : NCB * Q_CHUNK;   // a pair keeps Q in TMEM
+  static constexpr int Q_LOAD_BYTES = NCB * Q_CHUNK;        // one TMA load of this CTA's Q columns
+  static constexpr int Q_BYTES = PAIR ? 0 : Q_LOAD_BYTES;    // a pair keeps Q in TMEM
   static constexpr int KV_BYTES = NCB * KV_CHUNK;
   static constexpr int X_BYTES = PAIR ? kRows * kKeys * 4 : 0;  // one block's partial scores (f32)
   static constexpr int OFF_Q = 0;
@@ -114,6 +117,7 @@ struct PCfg {
   static_assert(OFF_K % 1024 == 0 && OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && KV_BYTES % 1024 == 0,
                 "1024-byte aligned operands");
   static_assert(COL_END <= TMEM_COLS, "TMEM budget");
+  static_assert(!PAIR || 2 * X_BYTES >= Q_LOAD_BYTES, "pair: Q is staged in the send and receive slots");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -126,7 +130,6 @@ struct PrefillParams {
   float scale_log2;      // scale * log2(e)
   uint32_t window;       // 0 = causal over the whole prefix
   int* err;
-  const uint16_t* q16;   // pair: [T, nqh, 2 HD] f16 queries (read into TMEM)
 };
 
 // --------------------------------------------------------------------------- tcgen05 helpers
@@ -358,6 +361,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
   uint64_t* barRx = bars + 35;      // pair: [4 quarters] the partner's partial scores landed
   uint64_t* barOK = bars + 39;      // pair: [4 quarters] the partner has read this CTA's
   uint64_t* barSx = bars + 43;      // pair: [2 parities][4 quarters] the full scores of block j in S[j % 2]
+  uint64_t* barQ2 = bars + 51;      // pair: Q copied from the slots into TMEM (4 exchange warps)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -396,13 +400,14 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
         g4a::mbar_init(&barOK[i], 1);  // the partner's exchange warp (remote arrival)
       }
       for (int i = 0; i < 8; i++) g4a::mbar_init(&barSx[i], 1);
+      g4a::mbar_init(barQ2, 4);
     }
-    g4a::mbar_init(barQ, PAIR ? 8 : 1);  // pair: the 8 softmax warps write Q into TMEM
+    g4a::mbar_init(barQ, 1);
     g4a::mbar_init(barEnd, 1);
     g4a::mbar_init(barEnd2, 1);
     *abort_flag = 0;
     g4a::fence_mbar_init();
-    if (!PAIR) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmq)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmo)) : "memory");
@@ -431,11 +436,12 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       const bool kside = warp == 0;
       uint64_t pol_kv;
       asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_kv));
-      if (kside && !PAIR) {
+      if (kside) {  // pair: this CTA's chunks of the Q tile, into the (still idle) exchange slots
         uint64_t pol_q;
         asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_q));
-        g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_BYTES);
-        tma_load_4d_p(sbase + C::OFF_Q, &tmq, 0, kvh * kHeadsPerKv, t0, 0, barQ, pol_q);
+        g4a::mbar_arrive_expect_tx(barQ, (uint32_t)C::Q_LOAD_BYTES);
+        tma_load_4d_p(sbase + (PAIR ? C::OFF_XS : C::OFF_Q), &tmq, 0, kvh * kHeadsPerKv, t0, (int)cr * C::NCB, barQ,
+                      pol_q);
       }
       uint64_t* empty = kside ? emptyK : emptyV;
       uint64_t* full = kside ? fullK : fullV;
@@ -453,7 +459,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
       // Loads still in flight land before the CTA retires (bounded).
       for (int j = max(0, nb - 2); j < nb; j++)
         (void)wait_or_abort(&full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
-      if (kside && !PAIR) (void)wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+      if (kside) (void)wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
     }
   } else if (warp == 1 || warp == 3) {
     // ------------------------------------------------------------------ MMA issuers
@@ -467,7 +473,7 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
         constexpr uint32_t idesc_s = f16_idesc(kKeys, false);
         const uint64_t dq = sw128_desc(sbase + C::OFF_Q, 16, 1024);
         const uint64_t dk0 = sw128_desc(sbase + C::OFF_K, 16, 1024);
-        bool ok = wait_or_abort(barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
+        bool ok = wait_or_abort(PAIR ? barQ2 : barQ, 0, abort_flag, p.err, G4A_DEVERR_WAIT_FULL);
         for (int j = 0; ok && j < nb; j++) {
           const int b = j & 1;
           // S[b] was last read out by the softmax of block j-2
@@ -538,32 +544,6 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
     float* alpha_buf = reinterpret_cast<float*>(smem + C::OFF_ALPHA);
     int* flag_buf = reinterpret_cast<int*>(smem + C::OFF_FLAG);
     const float c2 = p.scale_log2;
-    if constexpr (PAIR) {
-      // The Q tile into TMEM: row r = token t0 + r / 8, head kvh * 8 + r % 8; this CTA's head
-      // dims [HD cr, HD cr + HD), of which this half of the row's threads writes HD / 2.
-      const int qhead = kvh * kHeadsPerKv + r % kHeadsPerKv;
-      const uint4* src =
-          (tok < p.T) ? reinterpret_cast<const uint4*>(p.q16 + ((size_t)tok * p.nqh + qhead) * (2 * HD) + cr * HD +
-                                                       half * (HD / 2))
-                      : nullptr;
-#pragma unroll
-      for (int c = 0; c < HD / 128; c++) {  // 64 dims = 32 columns per store
-        uint32_t w[32];
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const uint4 v = src ? __ldg(src + 8 * c + i) : make_uint4(0u, 0u, 0u, 0u);
-          w[4 * i] = v.x;
-          w[4 * i + 1] = v.y;
-          w[4 * i + 2] = v.z;
-          w[4 * i + 3] = v.w;
-        }
-        tmem_st32(tmem + lane_addr + C::COL_Q + (uint32_t)(half * (HD / 4) + 32 * c), w);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) g4a::mbar_arrive(barQ);
-    }
     float m = -INFINITY;
     float lsum = 0.f;  // this half's share of the row sum, relative to m
     bool ok = true;
@@ -795,18 +775,44 @@ __global__ void __launch_bounds__(PCfg<HD, PAIR>::THREADS, 1)
     const uint32_t xr_peer = mapa_shared(xr, peer);
     const uint32_t rx_peer = mapa_shared(g4a::smem_u32(&barRx[quarter]), peer);
     const uint32_t ok_peer = mapa_shared(g4a::smem_u32(&barOK[quarter]), peer);
-    bool ok = true;
-    for (int j = 0; j < nb; j++) {
+    // Q into TMEM: row r = 32 quarter + lane (token t0 + r / 8, head kvh * 8 + r % 8), this CTA's
+    // 64-dim chunks c = 0..3 as landed by the TMA load ([chunk][128 rows][128 B], 16-byte unit k
+    // of row r at k ^ (r & 7)); dims 64 c + 8 k .. + 7 go to TMEM columns 32 c + 4 k .. + 3.
+    bool ok = warp_wait(barQ, 0u, abort_flag, p.err);
+    if (ok) {
+      const int r = quarter * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < C::NCB; c++) {
+        uint32_t w[32];
+        const uint32_t row = sbase + C::OFF_XS + (uint32_t)c * C::Q_CHUNK + (uint32_t)r * 128u;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w[4 * k]), "=r"(w[4 * k + 1]), "=r"(w[4 * k + 2]), "=r"(w[4 * k + 3])
+                       : "r"(row + (uint32_t)((k ^ (r & 7)) << 4))
+                       : "memory");
+        tmem_st32(tmem + lane_addr + C::COL_Q + (uint32_t)(32 * c), w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+    }
+    // every exchange warp has read the slots before any of them stages scores there, and the
+    // partner may copy its first scores into this CTA's receive slot (barOK phase 0)
+    g4a::named_bar_sync(2, 4 * 32);
+    if (ok && lane == 0) {
+      g4a::mbar_arrive(barQ2);
+      mbar_arrive_remote_relaxed(ok_peer);
+    }
+    for (int j = 0; ok && j < nb; j++) {
       const int b = j & 1;
       ok = warp_wait(&barS[b], (uint32_t)(j >> 1) & 1u, abort_flag, p.err);
       if (!ok) break;
       tc_fence_after();
       const uint32_t scol = tmem + lane_addr + C::COL_S + (uint32_t)(b * kKeys);
-      // the partner has read block j-1 from its slot, so the copy from xs has landed
-      if (j >= 1) {
-        ok = warp_wait_peer(&barOK[quarter], (uint32_t)(j - 1) & 1u, abort_flag, p.err);
-        if (!ok) break;
-      }
+      // the partner has read block j-1 from its slot (phase 0: its Q), so its receive slot is free
+      // and the copy from xs has landed
+      ok = warp_wait_peer(&barOK[quarter], (uint32_t)j & 1u, abort_flag, p.err);
+      if (!ok) break;
 #pragma unroll 1
       for (int h = 0; h < 2; h++) {  // 32 keys at a time (registers)
         uint32_t own[32];
@@ -935,10 +941,8 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   // pair: each CTA loads its NCB of the HD / 64 chunks of a K or V block (Q is read into TMEM)
   if (g4a_status s = encode_rows_map(ctx, &mk, k, HD, nkh, rows, 1, kKeys, C::NCB, "the K cache")) return s;
   if (g4a_status s = encode_rows_map(ctx, &mv, v, HD, nkh, rows, 1, kKeys, C::NCB, "the V cache")) return s;
-  if (kPair)
-    mq = mk;  // unused
-  else if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, C::NCB, "q16"))
-    return s;
+  // pair: each CTA loads its NCB of the HD / 64 chunks of the Q tile
+  if (g4a_status s = encode_rows_map(ctx, &mq, q16, HD, nqh, T, kHeadsPerKv, kTokPerTile, C::NCB, "q16")) return s;
   CUtensorMap mo;
   if (g4a_status s = encode_out_map(ctx, &mo, out, HD, nqh, T)) return s;
   PrefillParams p = {};
@@ -951,7 +955,6 @@ g4a_status launch_prefill(g4a_ctx* ctx, const uint16_t* q16, const uint16_t* k, 
   p.scale_log2 = scale * kLog2eP;
   p.window = window;
   p.err = ctx->dev_err_dev;
-  p.q16 = q16;
   g4a_prof_scope ps(ctx, G4A_PROF_PREFILL_ATTN);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(p.ntiles * p.nkh * (kPair ? 2 : 1)));
