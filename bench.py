@@ -215,7 +215,7 @@ def layers_for(L: int, cap: int = 64) -> int:
     return max(2, min(cap, math.ceil(4 * L2_BYTES / per)))
 
 
-def time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, steps, warmup):
+def time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, steps, warmup, window=0):
     """Capture one step (one call per layer cache) in a CUDA graph; replay warmup + steps times.
     Returns device ms for the timed steps."""
     R = len(kcs)
@@ -223,7 +223,7 @@ def time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, steps, warmup):
     def one_step():
         for r in range(R):
             ctx.decode_attn(qs[r], kcs[r], vcs[r], outs[r], num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
-                            seq_len=L, scale=1.0, sliding_window=0)
+                            seq_len=L, scale=1.0, sliding_window=window)
 
     one_step()  # configures kernels, sizes the workspace outside the capture
     torch.cuda.synchronize()
@@ -875,12 +875,15 @@ def run_projections(ctx, torch):
 
 
 def run_sweep(ctx, torch, args):
+    """4k and 128k global-layer contexts, and config[0]: a sliding-window layer (W = 512) at
+    kv_len 512 -- the shape of 28 of Gemma 4 E2B's 35 layers -- over 256 layer caches (138 MB of
+    visible KV per step, more than L2)."""
     out = {}
-    for L in (4096, 131072):
-        R = layers_for(L)
+    for L, W, cap in ((4096, 0, 64), (131072, 0, 64), (512, 512, 256)):
+        R = layers_for(L, cap)
         kcs, vcs, qs = build_layers(ctx, torch, L, R, seed=7)
         outs = [torch.zeros((NQH, HD), device="cuda") for _ in range(R)]
-        g = time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, 0, 3)
+        g = time_graph_steps(ctx, torch, kcs, vcs, qs, outs, L, 0, 3, window=W)
         steps = max(3, min(200, int(2e5 / R / max(L / 4096, 1))))
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -891,9 +894,9 @@ def run_sweep(ctx, torch, args):
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / (steps * R)
         hbm, _, _ = peaks()
-        gbs = kv_bytes(L) / (us * 1e-6) / 1e9
-        out[str(L)] = {"us_per_layer": us, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm, "layers": R,
-                       "steps": steps}
+        gbs = kv_bytes(L, W) / (us * 1e-6) / 1e9
+        out[f"sliding_{W}" if W else str(L)] = {"us_per_layer": us, "GB/s": gbs, "frac_of_measured_hbm": gbs / hbm,
+                                                "layers": R, "steps": steps, "kv_len": L, "window": W}
         del g, kcs, vcs
         torch.cuda.empty_cache()
     return out
