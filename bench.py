@@ -18,7 +18,8 @@ kernel -- timed in the graph vs the measured HBM copy peak, DRAM traffic per lau
 ncu capture),
 `e2e` (same metric through the C ABI, every layer call taking its q | k | v from pinned host
 memory and returning its output to pinned host memory), `cpu_baseline` (the CPU restatement of the reference chain on the host cores), `clocks`
-(nvidia-smi samples during the timed region) and `sweep` (4k / 128k contexts, N=1).
+(nvidia-smi samples during the timed region) and `sweep` (4k / 128k contexts and config[0]'s sliding-window
+layer, N=1).
 """
 from __future__ import annotations
 
