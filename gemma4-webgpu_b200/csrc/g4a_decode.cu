@@ -41,6 +41,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;  // 2 warps per SM sub-partition: up to 255 registers each
 constexpr float kLazyRescale = 8.0f;   // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kScanRegs = 4;           // problems per lane held in registers by the work-partition scans
 
 enum : int { F_SEG_FIRST = 1, F_SEG_LAST = 2, F_PROB_FIRST = 4, F_PROB_LAST = 8 };
 
@@ -79,9 +80,8 @@ __device__ __forceinline__ uint32_t seq_len_of(const DecodeParams& p, int seq) {
   return p.kv_lens ? (uint32_t)max(p.kv_lens[seq], 0) : p.kv_len_scalar;
 }
 
-// Visible key range [lo, hi) of a sequence (window measured from the full length).
-__device__ __forceinline__ void key_range(const DecodeParams& p, int seq, uint32_t& lo, uint32_t& hi) {
-  uint32_t L = seq_len_of(p, seq);
+// Visible key range [lo, hi) of a sequence of length L (window measured from the full length).
+__device__ __forceinline__ void key_range_of_len(const DecodeParams& p, uint32_t L, uint32_t& lo, uint32_t& hi) {
   if (p.page_table) {
     uint32_t cap = (uint32_t)p.max_pages * (uint32_t)p.page_size;
     if (L > cap) {
@@ -94,6 +94,9 @@ __device__ __forceinline__ void key_range(const DecodeParams& p, int seq, uint32
   lo = max(ws, p.row_base);
   hi = min(L, p.kv_end);
   if (hi < lo) hi = lo;
+}
+__device__ __forceinline__ void key_range(const DecodeParams& p, int seq, uint32_t& lo, uint32_t& hi) {
+  key_range_of_len(p, seq_len_of(p, seq), lo, hi);
 }
 
 // Address of the row of position t for (seq, kvh); null if its page id is out of range.
@@ -255,6 +258,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---- stage range [s0, s1) of this CTA over the flattened stage list (every warp computes it)
   long long S = 0;
+  // Non-uniform mode with at most 32 * kScanRegs problems: each lane keeps the stage counts of
+  // problems lane, lane + 32, ... in registers, so both scans below cost one round trip of
+  // kv_lens loads (issued together) instead of one per 32 problems and per scan.
+  const bool scan_regs = !uniform && P <= 32 * kScanRegs;
+  int cnt[kScanRegs];
   int nstg = 0;                // uniform mode: stages per problem
   uint32_t ulo = 0, uhi = 0;   // uniform mode: visible key range of every problem
   if (uniform) {
@@ -265,12 +273,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     // kv_lens, like q and the cache rows, may be written by the preceding kernel: with a
     // programmatic (PDL) launch, wait for it before reading any of them.
     g4a::pdl_wait_primary();
-    for (int base = 0; base < P; base += 32) {
-      const int pr = base + lane;
-      int n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
+    if (scan_regs) {
+      // all the loads first (a clamped index keeps them unconditional), then the counts
+      uint32_t len[kScanRegs];
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-      S += n;
+      for (int k = 0; k < kScanRegs; k++) len[k] = seq_len_of(p, min(32 * k + lane, P - 1) / p.nkh);
+#pragma unroll
+      for (int k = 0; k < kScanRegs; k++) {
+        uint32_t lo, hi;
+        key_range_of_len(p, len[k], lo, hi);
+        cnt[k] = (32 * k + lane < P && hi > lo) ? (int)((hi + KPS - 1) / KPS - lo / KPS) : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < kScanRegs; k++) {
+        int n = cnt[k];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+        S += n;
+      }
+    } else {
+      for (int base = 0; base < P; base += 32) {
+        const int pr = base + lane;
+        int n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+        S += n;
+      }
     }
   }
   // Only the first min(grid, S) CTAs take part, so every active CTA owns at least one stage and
@@ -307,7 +335,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool found = false;
     for (int base = 0; base < P && !found; base += 32) {
       const int pr = base + lane;
-      const int n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
+      int n = 0;
+      if (scan_regs) {
+#pragma unroll
+        for (int k = 0; k < kScanRegs; k++)
+          if (32 * k == base) n = cnt[k];
+      } else {
+        n = (pr < P) ? stages_of<KPS>(p, pr) : 0;
+      }
       int incl = n;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -521,16 +556,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         prob++;
       }
     } else {
-      for (int n = 0; n < n0; n++) issue(n);
+      // The first stage only: its page-table lookup is a dependent load, and every warp waits
+      // for warp 0 in stage_q; the second stage is issued right after.
+      if (n0 > 0) issue(0);
     }
   }
   stage_q();
+  if (warp == 0 && !(uniform && p.page_table == nullptr)) {
+    const int n0 = min(kStages - 1, my_stages);
+    for (int n = 1; n < n0; n++) issue(n);
+  }
 
   // =========================== consumer role (all warps)
   float o[NT][4];             // NT n-tiles of 8 output dims: rows g (hi part) and g+8 (lo part)
   float m_run = -INFINITY;    // running max of head g (base 2)
   float l_part = 0.f;         // this thread's share of the running sum of head g
   bool seg_whole_start = false;
+  bool q_ready = false;       // qv holds the q block of the next segment (loaded during a merge)
   int cprob = prob0, cj = j0; // uniform mode: consumer cursor
   // ldmatrix lanes: matrix mi = lane/8, row r8 = lane%8.  A stage tensor is a sequence of
   // sub-boxes of BR rows (BR = KPS, or the page size when pages are smaller), each holding its
@@ -577,7 +619,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (mt.flags & F_SEG_FIRST) {
       if (it > 0) {  // a later segment: its q block (the merge area is free again)
-        load_q(mt.problem);
+        if (!q_ready) load_q(mt.problem);
+        q_ready = false;
         stage_q();
       }
 #pragma unroll
@@ -682,6 +725,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- merge the NKG key groups of each output slice (tree over shared memory).  The
       // first barrier orders the q reads of the merge area before the tree's writes.
       g4a::named_bar_sync(1, kThreads);
+      // When another segment follows in this CTA, its q block is loaded now, so that the loads
+      // are in flight during the merge instead of stalling every warp at the next segment's
+      // start.  Its problem: the consumer cursor (uniform mode), or the metadata of stage it + 1,
+      // which warp 0 wrote before the barrier above (it issues two stages ahead).
+      if (it + 1 < my_stages) {
+        load_q(uniform ? cprob : meta[(it + 1) % kStages].problem);
+        q_ready = true;
+      }
       float l_head = l_part;
       l_head += __shfl_xor_sync(0xffffffffu, l_head, 1);
       l_head += __shfl_xor_sync(0xffffffffu, l_head, 2);
