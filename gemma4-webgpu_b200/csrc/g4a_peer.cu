@@ -63,24 +63,27 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, 
       st_release_sys(flags + par * world + rank, seq);
     }
   }
-  // ---- wait for every rank's slot in this rank's own buffer (bounded)
+  // ---- wait for every rank's slot in this rank's own buffer (bounded).  Lane j of warp 0 polls
+  // the flag of rank j, so the world acquire loads are in flight together rather than one after
+  // another (each is a system-scope round trip); the CTA barrier then orders every lane's
+  // acquire before the other threads' reads of the slots.
   __shared__ int ok;
-  if (tid == 0) {
+  if (tid < 32) {
     const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.buf[rank] + slots_floats) + par * world;
-    const uint64_t t0 = g4a::globaltimer_ns();
-    int good = 1;
-    uint32_t spins = 0;
-    for (int j = 0; j < world; j++) {
-      while (ld_acquire_sys(flags + j) != seq) {
+    bool good = true;
+    if (tid < world) {
+      const uint64_t t0 = g4a::globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_sys(flags + tid) != seq) {
         if ((++spins & 1023u) == 0u && g4a::globaltimer_ns() - t0 > 2000000000ull) {
-          good = 0;
+          good = false;
           if (err) atomicExch(err, G4A_DEVERR_WAIT_PEER);
           break;
         }
       }
-      if (!good) break;
     }
-    ok = good;
+    const bool all_good = __all_sync(0xffffffffu, good);
+    if (tid == 0) ok = all_good ? 1 : 0;
     __threadfence();
   }
   __syncthreads();
@@ -92,18 +95,22 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const float* part, 
     for (int d = tid; d < hd; d += blockDim.x) out[(size_t)h * hd + d] = 0.f;
     return;
   }
+  // every rank's (m, l) of head h loaded before any is used: one round trip, not one per rank
+  float mv[kMaxWorld], lv[kMaxWorld];
+#pragma unroll
+  for (int r = 0; r < kMaxWorld; r++) {
+    mv[r] = (r < world) ? __ldcg(base + (size_t)r * ps + h) : -INFINITY;
+    lv[r] = (r < world) ? __ldcg(base + (size_t)r * ps + nqh + h) : 0.f;
+  }
   float M = -INFINITY;
-  for (int r = 0; r < world; r++) M = fmaxf(M, __ldcg(base + (size_t)r * ps + h));
+#pragma unroll
+  for (int r = 0; r < kMaxWorld; r++) M = fmaxf(M, mv[r]);
   float L = 0.f;
   float w[kMaxWorld];
 #pragma unroll
   for (int r = 0; r < kMaxWorld; r++) {
-    w[r] = 0.f;
-    if (r < world) {
-      const float mr = __ldcg(base + (size_t)r * ps + h);
-      w[r] = (mr == -INFINITY) ? 0.f : exp2f(mr - M);
-      L += w[r] * __ldcg(base + (size_t)r * ps + nqh + h);
-    }
+    w[r] = (r < world && mv[r] != -INFINITY) ? exp2f(mv[r] - M) : 0.f;
+    L += w[r] * lv[r];
   }
   const float inv = (L > 0.f) ? 1.0f / L : 0.f;
   for (int d = tid; d < hd; d += blockDim.x) {
