@@ -65,6 +65,9 @@ def parse():
     ap.add_argument("--ncu-matmul", type=int, default=-1, metavar="FMT",
                     help="only run three lm-head sized GEMV launches (262144 x 1536) of weight format FMT "
                          "(0 f16, 1 Q8, 2 4-bit), for an ncu capture")
+    ap.add_argument("--ncu-paged", type=int, default=-1, metavar="W",
+                    help="small profiling workload: config[2]'s paged decode over the 64 sequences with sliding "
+                         "window W (512: the sliding layer, 0: the global layer), three launches, no timing")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the prefill, batched-paged and split-KV 1M measurements")
     ap.add_argument("--ncu-case", type=int, default=0, metavar="L",
@@ -952,6 +955,34 @@ def run_ncu_prefill(W: int, HD: int = HD) -> int:
     return 0
 
 
+def run_ncu_paged(W: int) -> int:
+    """Three launches of config[2]'s paged decode (B = 64, seeded lengths and page order) with
+    sliding window W, for ncu.  Only the pages the sequences use are allocated (~1.2 GB)."""
+    import numpy as np
+    import torch
+
+    import g4attn
+    from g4attn import synth
+
+    lens = synth.batched_lengths(2, 64, 1024, 32768).astype(np.int32)
+    with g4attn.Context(0) as ctx:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(40)
+        table, npages = synth.page_assignment(7 if W else 8, lens, 64)
+        kp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+        vp = torch.randn((npages, 64, NKH, HD), generator=g, device="cuda").half()
+        tb = torch.from_numpy(table).cuda()
+        q = torch.randn((len(lens), NQH, HD), generator=g, device="cuda")
+        out = torch.empty((len(lens), NQH, HD), device="cuda")
+        kvl = torch.from_numpy(lens.copy()).cuda()
+        for _ in range(3):
+            ctx.decode_attn_paged(q, kp, vp, tb, kvl, out, num_q_heads=NQH, num_kv_heads=NKH, head_dim=HD,
+                                  page_size=64, sliding_window=W, host_kv_lens=lens)
+        ctx.sync()
+        print(json.dumps({"ncu_paged": W, "out_abs_sum": float(out.abs().sum())}))
+    return 0
+
+
 def run_ncu_matmul(fmt: int) -> int:
     """Three launches of one lm-head sized GEMV (weights 252 MB at 4 bits, above L2), for ncu."""
     import torch
@@ -985,6 +1016,8 @@ def main():
         return run_ncu_prefill(args.ncu_prefill, args.ncu_head_dim)
     if args.ncu_matmul >= 0:
         return run_ncu_matmul(args.ncu_matmul)
+    if args.ncu_paged >= 0:
+        return run_ncu_paged(args.ncu_paged)
     if args.ncu_case:
         return run_ncu_case(args.ncu_case)
     if args.impl == "reference":
