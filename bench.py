@@ -91,7 +91,7 @@ def kv_bytes(L: int, window: int = 0) -> int:
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of decode_splitkv_kernel<256>
 # from an ncu capture of `python bench.py --ncu-case 32768` (cold L2 before each replay), keyed by
 # kv_len.  A prior capture, not a measurement of this run.
-DECODE_NCU_TRAFFIC = {32768: 33632000}
+DECODE_NCU_TRAFFIC = {32768: 33632512}
 
 
 def workload_config(L: int, world: int) -> dict:
